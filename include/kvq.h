@@ -1,0 +1,98 @@
+/*
+ * kvq.h - C ABI of the B200 (sm_100a) 4-bit KV-cache library (libkvq.so).
+ *
+ * Drop-in native layer under the Python entry points of the reference
+ * sztlink/krea-realtime-bench (quant_kv.py, quant_kv_kernels.py). Every entry
+ * point takes plain device pointers, sizes and a CUDA stream (passed as void*,
+ * a cudaStream_t; NULL = legacy default stream), launches asynchronously on that
+ * stream and returns 0 or a negative status. No exception crosses the ABI;
+ * kvq_last_error() returns the message of the calling thread's last failure.
+ *
+ * Cache storage (identical to the reference, quant_kv.py:107-111 and
+ * quant_kv_kernels.py:13-16):
+ *   codes   uint8 [S, H, D/2] int4: byte i = code(2i) | code(2i+1) << 4, code = q + 8
+ *           uint8 [S, H, D]   int8: code = q + 128
+ *   scales  bf16  [S, H, G]   one scale per (token, head, channel group)
+ *   sink    bf16  [sink, H, D] exact copy of the first `sink` tokens (optional)
+ * Channel groups are given by a HOST int32 array chan_band[D] (group index per
+ * channel, values in [0, G)), the array the reference builds on the device with
+ * build_chan_band (quant_kv_kernels.py:114-119). The five layouts the reference
+ * uses (bands, bands2, bands4, blind32, blind64; quant_kv.py:62-82) run on
+ * specialised kernels; any other map runs on a generic kernel with the same
+ * results.
+ */
+#ifndef KVQ_H_
+#define KVQ_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define KVQ_API __attribute__((visibility("default")))
+#else
+#define KVQ_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define KVQ_OK 0
+#define KVQ_ERR_ARG (-1)         /* invalid argument: shape, pointer, group map */
+#define KVQ_ERR_UNSUPPORTED (-2) /* valid but not supported by this build (e.g. head_dim) */
+#define KVQ_ERR_CUDA (-3)        /* a CUDA runtime call failed (message has the CUDA error) */
+#define KVQ_ERR_ALIGN (-4)       /* a pointer or stride is not aligned as required */
+#define KVQ_ERR_DEVICE (-5)      /* the current device is not an sm_100 part */
+
+/* ABI version of this header; bumped on any signature change. */
+#define KVQ_ABI_VERSION 1
+
+KVQ_API int kvq_abi_version(void);
+
+/* Message of the calling thread's last failing call ("" if none). */
+KVQ_API const char* kvq_last_error(void);
+
+/*
+ * Quantize rows of bf16 K or V into codes + scales, in place.
+ * Replaces: quant_kv_kernels.quantize (quant_kv_kernels.py:102-111), the Triton
+ * _quant_kernel launch (quant_kv_kernels.py:57-84) and the torch oracle
+ * QuantKVTensor._quantize (quant_kv.py:142-159). Codes and scales are bit-exact
+ * to the torch path (round half to even, IEEE divides), not to the Triton kernel.
+ *
+ *   x          bf16 [n_tokens][n_heads][head_dim], token stride x_token_stride
+ *              elements (>= n_heads*head_dim); 16-byte aligned rows
+ *   codes      uint8 out, [n_tokens][n_heads][head_dim/2] (bits 4) or [..][head_dim] (bits 8)
+ *   scales     bf16 out, [n_tokens][n_heads][n_groups]
+ *   sink       bf16 out or NULL: rows of x whose token index is < sink_tokens are
+ *              also copied verbatim to sink ([sink_tokens][n_heads][head_dim]),
+ *              as QuantKVTensor.__setitem__ does (quant_kv.py:213-215)
+ *   chan_band  HOST int32[head_dim], group of each channel
+ *   bits       4 or 8 (qmax 7 or 127)
+ */
+KVQ_API int kvq_quantize(const void* x, int64_t x_token_stride, void* codes, void* scales,
+                 void* sink, int64_t sink_tokens, int64_t n_tokens, int n_heads,
+                 int head_dim, const int32_t* chan_band, int n_groups, int bits,
+                 void* stream);
+
+/*
+ * Dequantize rows to bf16, optionally overlaying the exact sink copy.
+ * Replaces: quant_kv_kernels.dequantize (quant_kv_kernels.py:91-99), the Triton
+ * _dequant_kernel (quant_kv_kernels.py:33-55) and, with a sink, the read
+ * QuantKVTensor.__getitem__ (quant_kv.py:189-199). Bit-exact to the torch path.
+ *
+ *   codes, scales  as produced by kvq_quantize, first row = first token read
+ *   sink           bf16 or NULL; tokens < sink_tokens are copied from sink
+ *                  (sink points at the sink row of the first token read)
+ *   out            bf16 out [n_tokens][n_heads][head_dim], token stride
+ *                  out_token_stride elements
+ */
+KVQ_API int kvq_dequantize(const void* codes, const void* scales, const void* sink,
+                   int64_t sink_tokens, void* out, int64_t out_token_stride,
+                   int64_t n_tokens, int n_heads, int head_dim,
+                   const int32_t* chan_band, int n_groups, int bits, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KVQ_H_ */

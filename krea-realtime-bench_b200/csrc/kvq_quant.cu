@@ -1,0 +1,473 @@
+// Quantize-on-append / rebuild and dequantize kernels (sm_100a) + their C ABI.
+//
+// Reference semantics: QuantKVTensor._quantize / _dequantize (quant_kv.py:142-176),
+// torch path, bit-exact. The reference's Triton kernels (quant_kv_kernels.py:33-84)
+// round ties away from zero and are NOT the parity target.
+//
+// Quantize, specialised layouts (head_dim 128), one CTA of 128 threads per tile of
+// 128 (token, head) rows:
+//   1. the 32 KB input tile is loaded with coalesced 16-byte loads into shared
+//      memory, chunk c of row r stored at slot c ^ (r & 7), so that the per-row
+//      reads of step 2 are bank-conflict free;
+//   2. thread r owns row r: 64 bf16x2 words in registers, per-group absmax on
+//      packed bf16x2 (NaN-propagating), one IEEE divide and one correctly
+//      rounded reciprocal per group, then per element the division-free code
+//        y0 = x*r, rem = fma(-y0, s, x), y = fma(rem, r, y0), code = rne(y)
+//      which equals rne(x / s) for every finite bf16 pair (x, amax) with
+//      amax >= 2^-100 (exhaustively checked by the oracle's
+//      kvqo_check_fast_codes); other groups use the exact divide;
+//      rne and the +8 / +128 offset come from one add of a magic constant;
+//   3. codes and scales are staged in shared memory and written out with
+//      coalesced stores; rows inside the sink are copied to the bf16 sink buffer
+//      from the staged input.
+// Any other group map runs quantize_rows_generic (one warp per row, shared-memory
+// atomics for the per-group max), with the same results.
+#include <utility>
+
+#include "kvq_common.cuh"
+
+namespace kvq {
+
+constexpr int kQT = 128;  // threads per CTA = rows per tile (fast quantize)
+constexpr int kQD = 128;  // head_dim of the specialised kernels
+
+struct QuantArgs {
+  const uint16_t* x;
+  int64_t x_token_stride;  // elements
+  uint8_t* codes;
+  uint16_t* scales;
+  uint16_t* sink;
+  int64_t n_rows;     // n_tokens * H
+  int64_t sink_rows;  // rows of x that are also copied to sink
+  int H;
+  int rows_contig;  // x_token_stride == H * D
+};
+
+__device__ __forceinline__ const uint16_t* x_row_ptr(const QuantArgs& a, int64_t row, int D) {
+  if (a.rows_contig) return a.x + row * D;
+  int64_t t = row / a.H;
+  int h = static_cast<int>(row - t * a.H);
+  return a.x + t * a.x_token_stride + static_cast<int64_t>(h) * D;
+}
+
+// Absolute values of a bf16x2 word, max'ed into m with NaN propagation.
+__device__ __forceinline__ uint32_t absmax_bf16x2(uint32_t m, uint32_t w) {
+  uint32_t a = w & 0x7FFF7FFFu;
+  uint32_t r;
+  asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(m), "r"(a));
+  return r;
+}
+
+// Division-free code of x: returns the bit pattern of rne(x/s) + magic, whose low
+// byte is the offset code (see file comment). `fast` groups only.
+__device__ __forceinline__ uint32_t code_fast(float x, float s, float r, float magic) {
+  float y0 = __fmul_rn(x, r);
+  float rem = __fmaf_rn(-y0, s, x);
+  float y = __fmaf_rn(rem, r, y0);
+  return __float_as_uint(__fadd_rn(y, magic));
+}
+
+// Reference formula with the IEEE divide; clamps so non-finite inputs give codes
+// in range (they are outside the parity contract).
+__device__ __forceinline__ uint32_t code_exact(float x, float s, float qmax, float magic) {
+  float y = __fdiv_rn(x, s);
+  y = fminf(fmaxf(y, -qmax), qmax);
+  return __float_as_uint(__fadd_rn(y, magic));
+}
+
+template <int BITS>
+struct QuantConsts {
+  static constexpr int kQmax = (1 << (BITS - 1)) - 1;
+  // 1.5 * 2^23 + offset: adding it rounds to the nearest even integer and puts
+  // code + offset in the low bits of the result.
+  static constexpr float kMagic = 12582912.0f + (BITS == 4 ? 8.0f : 128.0f);
+  static constexpr int kCodeBytes = BITS == 4 ? kQD / 2 : kQD;  // per row
+};
+
+template <int LO, int HI, int BITS>
+__device__ __forceinline__ void quant_group(const uint32_t (&w)[64], uint32_t (&ow)[BITS == 4 ? 16 : 32],
+                                            uint16_t& scale_out) {
+  using C = QuantConsts<BITS>;
+  static_assert(LO % 2 == 0 && HI % 2 == 0 && LO < HI, "groups must start and end on even channels");
+  uint32_t m = 0;
+#pragma unroll
+  for (int k = LO / 2; k < HI / 2; ++k) m = absmax_bf16x2(m, w[k]);
+  float amax;
+  {
+    uint32_t lo = m << 16, hi = m & 0xFFFF0000u;
+    float a = __uint_as_float(lo), b = __uint_as_float(hi);
+    amax = (a != a || b != b) ? __uint_as_float(0x7FC00000u) : fmaxf(a, b);
+  }
+  float s = __fdiv_rn(amax, static_cast<float>(C::kQmax));
+  s = (s > 0.0f) ? s : 1.0f;  // quant_kv.py:152 (also maps NaN to 1, like torch.where)
+  scale_out = f32_to_bf16_bits(s);
+  const bool fast = (amax >= 0x1p-100f) && (amax <= 3.0e38f);
+  if (fast) {
+    const float r = __frcp_rn(s);
+#pragma unroll
+    for (int k = LO / 2; k < HI / 2; ++k) {
+      uint32_t c0 = code_fast(bf16lo_to_f32(w[k]), s, r, C::kMagic);
+      uint32_t c1 = code_fast(bf16hi_to_f32(w[k]), s, r, C::kMagic);
+      if constexpr (BITS == 4) {
+        uint32_t byte = (c0 & 0xFu) | ((c1 & 0xFu) << 4);
+        ow[k >> 2] |= byte << (8 * (k & 3));
+      } else {
+        uint32_t half = (c0 & 0xFFu) | ((c1 & 0xFFu) << 8);
+        ow[k >> 1] |= half << (16 * (k & 1));
+      }
+    }
+  } else {
+    const float q = static_cast<float>(C::kQmax);
+#pragma unroll
+    for (int k = LO / 2; k < HI / 2; ++k) {
+      uint32_t c0 = code_exact(bf16lo_to_f32(w[k]), s, q, C::kMagic);
+      uint32_t c1 = code_exact(bf16hi_to_f32(w[k]), s, q, C::kMagic);
+      if constexpr (BITS == 4) {
+        uint32_t byte = (c0 & 0xFu) | ((c1 & 0xFu) << 4);
+        ow[k >> 2] |= byte << (8 * (k & 3));
+      } else {
+        uint32_t half = (c0 & 0xFFu) | ((c1 & 0xFFu) << 8);
+        ow[k >> 1] |= half << (16 * (k & 1));
+      }
+    }
+  }
+}
+
+template <class L, int BITS, int... Gs>
+__device__ __forceinline__ void quant_row(const uint32_t (&w)[64], uint32_t (&ow)[BITS == 4 ? 16 : 32],
+                                          uint16_t (&sc)[L::G], std::integer_sequence<int, Gs...>) {
+  (quant_group<L::E[Gs], L::E[Gs + 1], BITS>(w, ow, sc[Gs]), ...);
+}
+
+template <class L, int BITS>
+__global__ void __launch_bounds__(kQT) quantize_rows_fast(QuantArgs a) {
+  using C = QuantConsts<BITS>;
+  constexpr int G = L::G;
+  constexpr int CW = C::kCodeBytes;           // code bytes per row
+  constexpr int CCH = CW / 16;                // 16-byte code chunks per row
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint4* sm_in = reinterpret_cast<uint4*>(smem_raw);                       // kQT * 16 chunks
+  uint4* sm_codes = reinterpret_cast<uint4*>(smem_raw + kQT * 256);        // kQT * CCH chunks
+  uint16_t* sm_sc = reinterpret_cast<uint16_t*>(smem_raw + kQT * 256 + kQT * CW);  // kQT * G
+
+  const int64_t row0 = static_cast<int64_t>(blockIdx.x) * kQT;
+  const int nrows = static_cast<int>(min(static_cast<int64_t>(kQT), a.n_rows - row0));
+  const int tid = threadIdx.x;
+
+  // 1. coalesced tile load
+#pragma unroll 8
+  for (int i = tid; i < nrows * 16; i += kQT) {
+    const int r = i >> 4, c = i & 15;
+    const uint16_t* src = x_row_ptr(a, row0 + r, kQD) + c * 8;
+    sm_in[r * 16 + (c ^ (r & 7))] = ld_global_nc_v4(src);
+  }
+  __syncthreads();
+
+  // 2. one row per thread
+  if (tid < nrows) {
+    uint32_t w[64];
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+      uint4 v = sm_in[tid * 16 + (c ^ (tid & 7))];
+      w[4 * c + 0] = v.x;
+      w[4 * c + 1] = v.y;
+      w[4 * c + 2] = v.z;
+      w[4 * c + 3] = v.w;
+    }
+    uint32_t ow[BITS == 4 ? 16 : 32];
+#pragma unroll
+    for (int k = 0; k < (BITS == 4 ? 16 : 32); ++k) ow[k] = 0;
+    uint16_t sc[G];
+    quant_row<L, BITS>(w, ow, sc, std::make_integer_sequence<int, G>{});
+    // stage codes: chunk c of row r at slot c ^ swz(r) (conflict-free both ways)
+#pragma unroll
+    for (int c = 0; c < CCH; ++c) {
+      const int slot = (BITS == 4) ? (c ^ ((tid >> 1) & 3)) : (c ^ (tid & 7));
+      sm_codes[tid * CCH + slot] = make_uint4(ow[4 * c], ow[4 * c + 1], ow[4 * c + 2], ow[4 * c + 3]);
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) sm_sc[tid * G + g] = sc[g];
+  }
+  __syncthreads();
+
+  // 3a. codes: nrows * CW contiguous bytes
+  {
+    uint4* dst = reinterpret_cast<uint4*>(a.codes + row0 * CW);
+    for (int i = tid; i < nrows * CCH; i += kQT) {
+      const int r = i / CCH, c = i % CCH;
+      const int slot = (BITS == 4) ? (c ^ ((r >> 1) & 3)) : (c ^ (r & 7));
+      st_global_v4(dst + i, sm_codes[r * CCH + slot]);
+    }
+  }
+  // 3b. scales: nrows * G contiguous bf16, any 2-byte alignment
+  {
+    uint16_t* dst = a.scales + row0 * G;
+    const int n = nrows * G;
+    if ((reinterpret_cast<uintptr_t>(dst) & 15) == 0 && (n % 8) == 0) {
+      const uint4* s4 = reinterpret_cast<const uint4*>(sm_sc);
+      for (int i = tid; i < n / 8; i += kQT) st_global_v4(reinterpret_cast<uint4*>(dst) + i, s4[i]);
+    } else if ((reinterpret_cast<uintptr_t>(dst) & 3) == 0 && (n % 2) == 0) {
+      const uint32_t* s2 = reinterpret_cast<const uint32_t*>(sm_sc);
+      for (int i = tid; i < n / 2; i += kQT) reinterpret_cast<uint32_t*>(dst)[i] = s2[i];
+    } else {
+      for (int i = tid; i < n; i += kQT) dst[i] = sm_sc[i];
+    }
+  }
+  // 3c. sink rows: exact bf16 copy (quant_kv.py:213-215)
+  if (a.sink != nullptr && row0 < a.sink_rows) {
+    const int ns = static_cast<int>(min(static_cast<int64_t>(nrows), a.sink_rows - row0));
+    uint4* dst = reinterpret_cast<uint4*>(a.sink + row0 * kQD);
+    for (int i = tid; i < ns * 16; i += kQT) {
+      const int r = i >> 4, c = i & 15;
+      st_global_v4(dst + i, sm_in[r * 16 + (c ^ (r & 7))]);
+    }
+  }
+}
+
+// ---------------------------------------------------------------- generic quantize
+constexpr int kGW = 8;  // warps per CTA
+
+__global__ void __launch_bounds__(kGW * 32) quantize_rows_generic(QuantArgs a, GroupMap map, int D, int G,
+                                                                  int bits) {
+  __shared__ uint32_t gmax[kGW][kMaxGroups];
+  __shared__ uint8_t gid[kMaxHeadDim];
+  for (int c = threadIdx.x; c < D; c += blockDim.x) gid[c] = map.gid[c];
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qmax = (1 << (bits - 1)) - 1;
+  const float qf = static_cast<float>(qmax);
+  const float magic = 12582912.0f + (bits == 4 ? 8.0f : 128.0f);
+  const int cw = bits == 4 ? D / 2 : D;
+  for (int64_t row = static_cast<int64_t>(blockIdx.x) * kGW + warp; row < a.n_rows;
+       row += static_cast<int64_t>(gridDim.x) * kGW) {
+    for (int g = lane; g < G; g += 32) gmax[warp][g] = 0u;
+    __syncwarp();
+    const uint32_t* src = reinterpret_cast<const uint32_t*>(x_row_ptr(a, row, D));
+    for (int p = lane; p < D / 2; p += 32) {
+      uint32_t wv = src[p];
+      atomicMax(&gmax[warp][gid[2 * p]], (wv << 16) & 0x7FFF0000u);
+      atomicMax(&gmax[warp][gid[2 * p + 1]], wv & 0x7FFF0000u);
+    }
+    __syncwarp();
+    for (int p = lane; p < D / 2; p += 32) {
+      uint32_t wv = src[p];
+      float x0 = bf16lo_to_f32(wv), x1 = bf16hi_to_f32(wv);
+      float s0 = __fdiv_rn(__uint_as_float(gmax[warp][gid[2 * p]]), qf);
+      float s1 = __fdiv_rn(__uint_as_float(gmax[warp][gid[2 * p + 1]]), qf);
+      s0 = (s0 > 0.0f) ? s0 : 1.0f;
+      s1 = (s1 > 0.0f) ? s1 : 1.0f;
+      uint32_t c0 = code_exact(x0, s0, qf, magic), c1 = code_exact(x1, s1, qf, magic);
+      if (bits == 4) {
+        a.codes[row * cw + p] = static_cast<uint8_t>((c0 & 0xFu) | ((c1 & 0xFu) << 4));
+      } else {
+        reinterpret_cast<uint16_t*>(a.codes + row * cw)[p] =
+            static_cast<uint16_t>((c0 & 0xFFu) | ((c1 & 0xFFu) << 8));
+      }
+      if (a.sink != nullptr && row < a.sink_rows) reinterpret_cast<uint32_t*>(a.sink + row * D)[p] = wv;
+    }
+    for (int g = lane; g < G; g += 32) {
+      float s = __fdiv_rn(__uint_as_float(gmax[warp][g]), qf);
+      s = (s > 0.0f) ? s : 1.0f;
+      a.scales[row * G + g] = f32_to_bf16_bits(s);
+    }
+    __syncwarp();
+  }
+}
+
+// ---------------------------------------------------------------- dequantize
+struct DequantArgs {
+  const uint8_t* codes;
+  const uint16_t* scales;
+  const uint16_t* sink;
+  int64_t sink_rows;
+  uint16_t* out;
+  int64_t out_token_stride;
+  int64_t n_rows;
+  int H, D, G, bits;
+  int rows_contig;
+};
+
+// One thread per 8 channels of a row: reads 4 (int4) or 8 (int8) code bytes and
+// the row's scales, writes 16 bytes of bf16. bf16((q) * float(scale)) is exact in
+// fp32 before the final round to nearest even, as in quant_kv.py:174-175.
+__global__ void __launch_bounds__(256) dequantize_rows(DequantArgs a, GroupMap map) {
+  __shared__ uint8_t gid[kMaxHeadDim];
+  for (int c = threadIdx.x; c < a.D; c += blockDim.x) gid[c] = map.gid[c];
+  __syncthreads();
+  const int cpr = a.D / 8;
+  const int64_t total = a.n_rows * cpr;
+  for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t row = idx / cpr;
+    const int c8 = static_cast<int>(idx - row * cpr);
+    uint16_t* dst;
+    if (a.rows_contig) {
+      dst = a.out + row * a.D + c8 * 8;
+    } else {
+      int64_t t = row / a.H;
+      int h = static_cast<int>(row - t * a.H);
+      dst = a.out + t * a.out_token_stride + static_cast<int64_t>(h) * a.D + c8 * 8;
+    }
+    if (a.sink != nullptr && row < a.sink_rows) {
+      st_global_v4(dst, *reinterpret_cast<const uint4*>(a.sink + row * a.D + c8 * 8));
+      continue;
+    }
+    int q[8];
+    if (a.bits == 4) {
+      uint32_t wv = *reinterpret_cast<const uint32_t*>(a.codes + row * (a.D / 2) + c8 * 4);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) q[k] = static_cast<int>((wv >> (4 * k)) & 0xFu) - 8;
+    } else {
+      uint2 wv = *reinterpret_cast<const uint2*>(a.codes + row * a.D + c8 * 8);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        q[k] = static_cast<int>((wv.x >> (8 * k)) & 0xFFu) - 128;
+        q[4 + k] = static_cast<int>((wv.y >> (8 * k)) & 0xFFu) - 128;
+      }
+    }
+    const uint16_t* srow = a.scales + row * a.G;
+    float v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      v[k] = __fmul_rn(static_cast<float>(q[k]), bf16_bits_to_f32(srow[gid[c8 * 8 + k]]));
+    st_global_v4(dst, make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]),
+                                 pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7])));
+  }
+}
+
+static int num_sms() {
+  static int sms[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (sms[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    sms[dev] = n;
+  }
+  return sms[dev];
+}
+
+template <class L, int BITS>
+static int launch_fast(const QuantArgs& a, cudaStream_t st) {
+  constexpr int smem = kQT * 256 + kQT * QuantConsts<BITS>::kCodeBytes + ((kQT * L::G * 2 + 15) / 16) * 16;
+  static_assert(smem <= 227 * 1024, "tile too large");
+  // opt in to > 48 KB of dynamic shared memory once per device
+  static bool configured[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(quantize_rows_fast<L, BITS>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) {
+      set_error("cudaFuncSetAttribute(quantize): %s", cudaGetErrorString(e));
+      return KVQ_ERR_CUDA;
+    }
+    configured[dev] = true;
+  }
+  const int64_t tiles = (a.n_rows + kQT - 1) / kQT;
+  quantize_rows_fast<L, BITS><<<static_cast<unsigned>(tiles), kQT, smem, st>>>(a);
+  return check_launch("kvq_quantize");
+}
+
+template <int BITS>
+static int dispatch_fast(int layout, const QuantArgs& a, cudaStream_t st) {
+  switch (layout) {
+    case kLayoutBands: return launch_fast<LayoutBands, BITS>(a, st);
+    case kLayoutBands2: return launch_fast<LayoutBands2, BITS>(a, st);
+    case kLayoutBands4: return launch_fast<LayoutBands4, BITS>(a, st);
+    case kLayoutBlind32: return launch_fast<LayoutBlind32, BITS>(a, st);
+    case kLayoutBlind64: return launch_fast<LayoutBlind64, BITS>(a, st);
+    default: break;
+  }
+  set_error("internal: no specialised kernel for layout %d", layout);
+  return KVQ_ERR_UNSUPPORTED;
+}
+
+}  // namespace kvq
+
+using namespace kvq;
+
+extern "C" int kvq_quantize(const void* x, int64_t x_token_stride, void* codes, void* scales, void* sink,
+                            int64_t sink_tokens, int64_t n_tokens, int n_heads, int head_dim,
+                            const int32_t* chan_band, int n_groups, int bits, void* stream) {
+  clear_error();
+  KVQ_REQUIRE(bits == 4 || bits == 8, KVQ_ERR_ARG, "bits must be 4 or 8, got %d", bits);
+  KVQ_REQUIRE(n_tokens >= 0 && n_heads > 0, KVQ_ERR_ARG, "bad shape: n_tokens %lld, n_heads %d",
+              (long long)n_tokens, n_heads);
+  GroupMap map;
+  int layout = resolve_layout(chan_band, head_dim, n_groups, &map);
+  if (layout < 0) return layout;
+  if (n_tokens == 0) return KVQ_OK;
+  KVQ_REQUIRE(x && codes && scales, KVQ_ERR_ARG, "NULL data pointer");
+  KVQ_REQUIRE(x_token_stride >= static_cast<int64_t>(n_heads) * head_dim, KVQ_ERR_ARG,
+              "x_token_stride %lld < n_heads*head_dim", (long long)x_token_stride);
+  KVQ_REQUIRE(sink_tokens >= 0, KVQ_ERR_ARG, "negative sink_tokens");
+  KVQ_REQUIRE((reinterpret_cast<uintptr_t>(x) & 15) == 0 && (x_token_stride % 8) == 0, KVQ_ERR_ALIGN,
+              "x must be 16-byte aligned with a token stride that is a multiple of 8 elements");
+  KVQ_REQUIRE((reinterpret_cast<uintptr_t>(codes) & 15) == 0, KVQ_ERR_ALIGN, "codes must be 16-byte aligned");
+  KVQ_REQUIRE((reinterpret_cast<uintptr_t>(scales) & 1) == 0, KVQ_ERR_ALIGN, "scales must be 2-byte aligned");
+  KVQ_REQUIRE(sink == nullptr || (reinterpret_cast<uintptr_t>(sink) & 15) == 0, KVQ_ERR_ALIGN,
+              "sink must be 16-byte aligned");
+  int rc = require_sm100();
+  if (rc) return rc;
+  QuantArgs a;
+  a.x = static_cast<const uint16_t*>(x);
+  a.x_token_stride = x_token_stride;
+  a.codes = static_cast<uint8_t*>(codes);
+  a.scales = static_cast<uint16_t*>(scales);
+  a.sink = static_cast<uint16_t*>(sink);
+  a.n_rows = n_tokens * n_heads;
+  a.sink_rows = (sink ? (sink_tokens < n_tokens ? sink_tokens : n_tokens) : 0) * n_heads;
+  a.H = n_heads;
+  a.rows_contig = x_token_stride == static_cast<int64_t>(n_heads) * head_dim;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (layout != kLayoutGeneric)
+    return bits == 4 ? dispatch_fast<4>(layout, a, st) : dispatch_fast<8>(layout, a, st);
+  const int64_t blocks = (a.n_rows + kGW - 1) / kGW;
+  const int grid = static_cast<int>(blocks < num_sms() * 8 ? blocks : num_sms() * 8);
+  quantize_rows_generic<<<grid, kGW * 32, 0, st>>>(a, map, head_dim, n_groups, bits);
+  return check_launch("kvq_quantize(generic)");
+}
+
+extern "C" int kvq_dequantize(const void* codes, const void* scales, const void* sink, int64_t sink_tokens,
+                              void* out, int64_t out_token_stride, int64_t n_tokens, int n_heads, int head_dim,
+                              const int32_t* chan_band, int n_groups, int bits, void* stream) {
+  clear_error();
+  KVQ_REQUIRE(bits == 4 || bits == 8, KVQ_ERR_ARG, "bits must be 4 or 8, got %d", bits);
+  KVQ_REQUIRE(n_tokens >= 0 && n_heads > 0, KVQ_ERR_ARG, "bad shape");
+  GroupMap map;
+  int layout = resolve_layout(chan_band, head_dim, n_groups, &map);
+  if (layout < 0) return layout;
+  if (n_tokens == 0) return KVQ_OK;
+  KVQ_REQUIRE(codes && scales && out, KVQ_ERR_ARG, "NULL data pointer");
+  KVQ_REQUIRE(out_token_stride >= static_cast<int64_t>(n_heads) * head_dim, KVQ_ERR_ARG,
+              "out_token_stride too small");
+  KVQ_REQUIRE(sink_tokens >= 0, KVQ_ERR_ARG, "negative sink_tokens");
+  KVQ_REQUIRE((reinterpret_cast<uintptr_t>(out) & 15) == 0 && (out_token_stride % 8) == 0, KVQ_ERR_ALIGN,
+              "out must be 16-byte aligned with a token stride that is a multiple of 8 elements");
+  KVQ_REQUIRE((reinterpret_cast<uintptr_t>(codes) & 7) == 0, KVQ_ERR_ALIGN, "codes must be 8-byte aligned");
+  KVQ_REQUIRE((reinterpret_cast<uintptr_t>(scales) & 1) == 0, KVQ_ERR_ALIGN, "scales must be 2-byte aligned");
+  KVQ_REQUIRE(sink == nullptr || (reinterpret_cast<uintptr_t>(sink) & 15) == 0, KVQ_ERR_ALIGN,
+              "sink must be 16-byte aligned");
+  int rc = require_sm100();
+  if (rc) return rc;
+  DequantArgs a;
+  a.codes = static_cast<const uint8_t*>(codes);
+  a.scales = static_cast<const uint16_t*>(scales);
+  a.sink = static_cast<const uint16_t*>(sink);
+  a.sink_rows = (sink ? (sink_tokens < n_tokens ? sink_tokens : n_tokens) : 0) * n_heads;
+  a.out = static_cast<uint16_t*>(out);
+  a.out_token_stride = out_token_stride;
+  a.n_rows = n_tokens * n_heads;
+  a.H = n_heads;
+  a.D = head_dim;
+  a.G = n_groups;
+  a.bits = bits;
+  a.rows_contig = out_token_stride == static_cast<int64_t>(n_heads) * head_dim;
+  const int64_t work = a.n_rows * (head_dim / 8);
+  const int64_t blocks = (work + 255) / 256;
+  const int grid = static_cast<int>(blocks < num_sms() * 16 ? blocks : num_sms() * 16);
+  dequantize_rows<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(a, map);
+  return check_launch("kvq_dequantize");
+}

@@ -1,0 +1,118 @@
+"""Torch-facing wrappers of the libkvq C ABI.
+
+Every op validates shapes/dtypes/devices on the host, passes raw device pointers
+to libkvq and launches on the current torch stream of the tensors' device. There
+is no CPU path: tensors on any device other than CUDA raise.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import torch
+
+from . import _lib
+
+
+def _stream(device: torch.device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _ptr(t: torch.Tensor | None) -> ctypes.c_void_p:
+    return ctypes.c_void_p(0 if t is None else t.data_ptr())
+
+
+def _host_map(chan_band) -> np.ndarray:
+    a = np.ascontiguousarray(np.asarray(chan_band, dtype=np.int32))
+    if a.ndim != 1:
+        raise ValueError("chan_band must be one-dimensional")
+    return a
+
+
+def _require_cuda(*ts: torch.Tensor | None) -> torch.device:
+    dev = None
+    for t in ts:
+        if t is None:
+            continue
+        if not isinstance(t, torch.Tensor):
+            raise TypeError(f"expected a torch.Tensor, got {type(t).__name__}")
+        if t.device.type != "cuda":
+            raise RuntimeError(
+                f"kvq ops run on CUDA (sm_100) tensors only; got a tensor on {t.device} "
+                "(the B200 build has no CPU path)")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise ValueError(f"tensors on different devices: {dev} and {t.device}")
+    return dev
+
+
+def _rows_view_ok(t: torch.Tensor, name: str, inner: int) -> int:
+    """[T, H, inner] with contiguous [H, inner] block; returns the token stride."""
+    if t.dim() != 3:
+        raise ValueError(f"{name} must be 3-D [tokens, heads, {inner}], got {tuple(t.shape)}")
+    if t.stride(2) != 1 or t.stride(1) != t.shape[2]:
+        raise ValueError(f"{name} must have a contiguous [heads, channels] block per token")
+    return t.stride(0)
+
+
+def quantize_into(x: torch.Tensor, codes: torch.Tensor, scales: torch.Tensor, chan_band,
+                  n_groups: int, bits: int = 4, sink: torch.Tensor | None = None,
+                  sink_tokens: int = 0) -> None:
+    """Quantize x [L, H, D] bf16 into codes/scales (views of any cache slice).
+
+    Rows of x with token index < sink_tokens are also copied to sink (which
+    points at the sink row of x's first token).
+    """
+    dev = _require_cuda(x, codes, scales, sink)
+    if x.dtype != torch.bfloat16:
+        raise TypeError(f"x must be bfloat16, got {x.dtype}")
+    L, H, D = x.shape
+    xs = _rows_view_ok(x, "x", D)
+    cw = D // 2 if bits == 4 else D
+    if codes.dtype != torch.uint8 or tuple(codes.shape) != (L, H, cw) or not codes.is_contiguous():
+        raise ValueError(f"codes must be contiguous uint8 {(L, H, cw)}, got {codes.dtype} {tuple(codes.shape)}")
+    if scales.dtype != torch.bfloat16 or tuple(scales.shape) != (L, H, n_groups) or not scales.is_contiguous():
+        raise ValueError(f"scales must be contiguous bf16 {(L, H, n_groups)}")
+    if sink is not None:
+        ns = min(sink_tokens, L)
+        if sink.dtype != torch.bfloat16 or sink.shape[0] < ns or tuple(sink.shape[1:]) != (H, D) \
+                or not sink.is_contiguous():
+            raise ValueError("sink must be contiguous bf16 [>=sink_tokens, H, D]")
+    cb = _host_map(chan_band)
+    if cb.shape[0] != D:
+        raise ValueError(f"chan_band has {cb.shape[0]} entries, head_dim is {D}")
+    with torch.cuda.device(dev):
+        rc = _lib.load().kvq_quantize(
+            _ptr(x), xs, _ptr(codes), _ptr(scales), _ptr(sink), int(sink_tokens) if sink is not None else 0,
+            L, H, D, cb.ctypes.data_as(ctypes.c_void_p), int(n_groups), int(bits), _stream(dev))
+    _lib.check(rc, "kvq_quantize")
+
+
+def dequantize_into(codes: torch.Tensor, scales: torch.Tensor, out: torch.Tensor, chan_band,
+                    n_groups: int, bits: int = 4, sink: torch.Tensor | None = None,
+                    sink_tokens: int = 0) -> torch.Tensor:
+    """Dequantize codes/scales [L, H, *] into out [L, H, D] bf16 (any token stride)."""
+    dev = _require_cuda(codes, scales, out, sink)
+    if out.dtype != torch.bfloat16:
+        raise TypeError(f"out must be bfloat16, got {out.dtype}")
+    L, H, D = out.shape
+    os_ = _rows_view_ok(out, "out", D)
+    cw = D // 2 if bits == 4 else D
+    if codes.dtype != torch.uint8 or tuple(codes.shape) != (L, H, cw) or not codes.is_contiguous():
+        raise ValueError(f"codes must be contiguous uint8 {(L, H, cw)}, got {codes.dtype} {tuple(codes.shape)}")
+    if scales.dtype != torch.bfloat16 or tuple(scales.shape) != (L, H, n_groups) or not scales.is_contiguous():
+        raise ValueError(f"scales must be contiguous bf16 {(L, H, n_groups)}")
+    if sink is not None and (sink.dtype != torch.bfloat16 or not sink.is_contiguous()
+                             or tuple(sink.shape[1:]) != (H, D) or sink.shape[0] < min(sink_tokens, L)):
+        raise ValueError("sink must be contiguous bf16 [>=sink_tokens, H, D]")
+    cb = _host_map(chan_band)
+    if cb.shape[0] != D:
+        raise ValueError(f"chan_band has {cb.shape[0]} entries, head_dim is {D}")
+    with torch.cuda.device(dev):
+        rc = _lib.load().kvq_dequantize(
+            _ptr(codes), _ptr(scales), _ptr(sink), int(sink_tokens) if sink is not None else 0,
+            _ptr(out), os_, L, H, D, cb.ctypes.data_as(ctypes.c_void_p), int(n_groups), int(bits),
+            _stream(dev))
+    _lib.check(rc, "kvq_dequantize")
+    return out

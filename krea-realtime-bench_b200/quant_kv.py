@@ -1,0 +1,359 @@
+"""Drop-in replacement for the reference's quant_kv.py on B200 (sm_100a).
+
+Same public surface as sztlink/krea-realtime-bench quant_kv.py:
+  FRAME_SEQ_LEN, ROPE_BANDS, HAVE_KERNELS, USE_KERNELS   quant_kv.py:50-59
+  _band_edges(head_dim, mode)                            quant_kv.py:62-82
+  QuantKVTensor(shape, device, dtype, bits, group_mode, sink_tokens)
+                                                         quant_kv.py:85-225
+  install(pipeline, k_bits, v_bits, group_mode, sink_frames, verbose)
+                                                         quant_kv.py:228-269
+plus the attention entry point that consumes the cache in packed form,
+`attention(q, k, v, ...)`, the call the runtime makes on a cache read
+(quant_kv.py:14; hook point probe_attention.py:97-124).
+
+Behaviour a caller can see, against the reference:
+  * slice writes quantize on the GPU straight into the cache slice (no
+    temporary + copy), codes/scales bit-exact to the reference torch path;
+  * slice reads `t[:, a:b]` return a QuantKVWindow, a lazy view of the packed
+    window. attention() reads it in packed form; any other use (a torch
+    function, a tensor method, `.clone()`) dequantizes it exactly as the
+    reference's __getitem__ does (quant_kv.py:189-199), sink overlay included;
+  * the leading dimension may be > 1: independent streams, each with its own
+    window (the reference asserts batch 1, quant_kv.py:95);
+  * there is no CPU path (the reference falls back to torch on CPU,
+    quant_kv.py:114): a non-CUDA device raises.
+"""
+from __future__ import annotations
+
+import os
+import warnings
+
+import numpy as np
+import torch
+
+import quant_kv_kernels as _kern
+from kvq import ops as _ops
+
+HAVE_KERNELS = _kern.HAVE_TRITON
+# no switch to a non-kernel path exists in this build
+USE_KERNELS = HAVE_KERNELS
+if os.environ.get("QKV_KERNELS", "1") == "0":
+    warnings.warn("QKV_KERNELS=0 is ignored: the B200 build has only the CUDA kernel path")
+
+FRAME_SEQ_LEN = 1560
+ROPE_BANDS = ((0, 44), (44, 86), (86, 128))
+
+
+def _band_edges(head_dim, mode):
+    """Channel groups (quant_kv.py:62-82): "bands" = the three rotary bands,
+    "bandsN" = each band cut in N pieces on even channels, "blindN" = fixed width."""
+    if mode.startswith("bands"):
+        assert head_dim == 128, f"rotary bands are mapped for head_dim 128, got {head_dim}"
+        n = int(mode[5:]) if len(mode) > 5 else 1
+        if n == 1:
+            return ROPE_BANDS
+        out = []
+        for lo, hi in ROPE_BANDS:
+            width = hi - lo
+            step = max(2, ((width + n - 1) // n + 1) // 2 * 2)
+            for s in range(lo, hi, step):
+                out.append((s, min(s + step, hi)))
+        return tuple(out)
+    if mode.startswith("blind"):
+        g = int(mode[5:])
+        return tuple((i, min(i + g, head_dim)) for i in range(0, head_dim, g))
+    raise ValueError(f"unknown group mode: {mode}")
+
+
+def _token_slice(idx):
+    """Accepts [:, a:b] and [:, a:b, ...] (quant_kv.py:179-187)."""
+    if not isinstance(idx, tuple):
+        raise TypeError("QuantKVTensor expects [:, a:b] indexing")
+    assert idx[0] == slice(None), "the batch dimension is always taken whole"
+    sl = idx[1]
+    assert isinstance(sl, slice) and sl.step in (None, 1), "contiguous slices only"
+    return sl
+
+
+class QuantKVTensor:
+    """Behaves like a [B, S, H, D] bf16 tensor across the runtime's operations.
+
+    Storage (reference layout, quant_kv.py:107-111; streams stacked along the
+    token axis, stream i owning rows [i*S, (i+1)*S)):
+      packed  uint8 [B*S, H, D/2] (int4) or [B*S, H, D] (int8)
+      scales  bf16  [B*S, H, G]
+      sink    bf16  [B*sink, H, D] or None
+    """
+
+    def __init__(self, shape, device, dtype=torch.bfloat16, bits=4,
+                 group_mode="bands", sink_tokens=0):
+        b, s, h, d = shape
+        assert b >= 1, "batch must be >= 1"
+        assert bits in (4, 8), "int4 or int8"
+        if dtype != torch.bfloat16:
+            raise TypeError(f"only bfloat16 caches are supported, got {dtype}")
+        dev = torch.device(device)
+        if dev.type != "cuda":
+            raise RuntimeError(f"QuantKVTensor needs a CUDA (sm_100) device, got {device}; "
+                               "the B200 build has no CPU path")
+        if dev.index is None:
+            dev = torch.device("cuda", torch.cuda.current_device())
+        self.logical_shape = torch.Size(shape)
+        self.dtype = dtype
+        self.device = dev
+        self.bits = bits
+        self.n_streams = b
+        self.n_tokens, self.n_heads, self.head_dim = s, h, d
+        self.bands = _band_edges(d, group_mode)
+        self.group_mode = group_mode
+        self.qmax = (1 << (bits - 1)) - 1
+        self.sink_tokens = min(sink_tokens, s)
+        packed_d = d // 2 if bits == 4 else d
+        self.packed = torch.zeros((b * s, h, packed_d), dtype=torch.uint8, device=dev)
+        self.scales = torch.zeros((b * s, h, len(self.bands)), dtype=dtype, device=dev)
+        self.sink = (torch.zeros((b * self.sink_tokens, h, d), dtype=dtype, device=dev)
+                     if self.sink_tokens else None)
+        self.use_kernels = True
+        self.chan_band = _kern.build_chan_band(self.bands, d, dev)
+        self.chan_band_host = np.ascontiguousarray(_kern.host_chan_band(self.chan_band))
+
+    # ------------------------------------------------------------------ tensor-like
+    @property
+    def shape(self):
+        return self.logical_shape
+
+    def size(self, dim=None):
+        return self.logical_shape if dim is None else self.logical_shape[dim]
+
+    def numel(self):
+        return int(self.logical_shape.numel())
+
+    def dim(self):
+        return 4
+
+    def zero_(self):
+        self.packed.zero_()
+        self.scales.zero_()
+        if self.sink is not None:
+            self.sink.zero_()
+        return self
+
+    def storage_bytes(self):
+        n = self.packed.numel() + self.scales.numel() * self.scales.element_size()
+        if self.sink is not None:
+            n += self.sink.numel() * self.sink.element_size()
+        return n
+
+    # ------------------------------------------------------------------ quant / dequant
+    def _quantize(self, x):
+        """x [L, H, D] bf16 -> (packed, scales), new tensors (quant_kv.py:142-159)."""
+        return _kern.quantize(x, self.chan_band, len(self.bands), self.qmax, self.dtype)
+
+    def _dequantize(self, packed, scales):
+        """(packed, scales) -> [L, H, D] bf16 (quant_kv.py:161-176)."""
+        return _kern.dequantize(packed, scales, self.chan_band, self.head_dim, self.dtype)
+
+    # ------------------------------------------------------------------ stream rows
+    def _rows(self, stream, a, b):
+        o = stream * self.n_tokens
+        return slice(o + a, o + b)
+
+    def _sink_rows(self, stream, a, b):
+        o = stream * self.sink_tokens
+        return slice(o + a, o + b)
+
+    def write_(self, a, b, value):
+        """Quantize value [B, b-a, H, D] (or [b-a, H, D] when B == 1) into tokens [a, b)."""
+        v = value
+        if v.dim() == 3:
+            v = v.unsqueeze(0)
+        assert v.dim() == 4 and v.shape[0] == self.n_streams, \
+            f"value has {v.shape[0]} streams, cache has {self.n_streams}"
+        assert v.shape[1] == b - a, f"write of {v.shape[1]} tokens into a slice of {b - a}"
+        if v.dtype != self.dtype:
+            v = v.to(self.dtype)
+        if v.device != self.device:
+            v = v.to(self.device)
+        G = len(self.bands)
+        ns = max(0, min(b, self.sink_tokens) - a) if self.sink is not None else 0
+        for i in range(self.n_streams):
+            x = v[i]
+            if x.stride(2) != 1 or x.stride(1) != self.head_dim or x.data_ptr() % 16 or x.stride(0) % 8:
+                x = x.contiguous()
+            rows = self._rows(i, a, b)
+            sink = self.sink[self._sink_rows(i, a, a + ns)] if ns > 0 else None
+            _ops.quantize_into(x, self.packed[rows], self.scales[rows], self.chan_band_host, G,
+                               self.bits, sink=sink, sink_tokens=ns)
+
+    def read(self, a, b, out=None):
+        """Dequantize tokens [a, b) with the sink overlay -> [B, b-a, H, D] bf16."""
+        B, H, D = self.n_streams, self.n_heads, self.head_dim
+        if out is None:
+            out = torch.empty((B, b - a, H, D), dtype=self.dtype, device=self.device)
+        ns = max(0, min(b, self.sink_tokens) - a) if self.sink is not None else 0
+        for i in range(B):
+            rows = self._rows(i, a, b)
+            sink = self.sink[self._sink_rows(i, a, a + ns)] if ns > 0 else None
+            _ops.dequantize_into(self.packed[rows], self.scales[rows], out[i], self.chan_band_host,
+                                 len(self.bands), self.bits, sink=sink, sink_tokens=ns)
+        return out
+
+    # ------------------------------------------------------------------ slicing
+    def __getitem__(self, idx):
+        sl = _token_slice(idx)
+        a, b, _ = sl.indices(self.n_tokens)
+        if b <= a:
+            return torch.empty((self.n_streams, 0, self.n_heads, self.head_dim),
+                               dtype=self.dtype, device=self.device)
+        return QuantKVWindow(self, a, b)
+
+    def __setitem__(self, idx, value):
+        sl = _token_slice(idx)
+        a, b, _ = sl.indices(self.n_tokens)
+        if b <= a:
+            return
+        if isinstance(value, QuantKVWindow):
+            value = value.materialize()
+        self.write_(a, b, value)
+
+    def clone(self):
+        raise RuntimeError("clone() on the whole cache is never called by the runtime")
+
+    def __repr__(self):
+        gb = self.storage_bytes() / 1e9
+        return (f"QuantKVTensor({tuple(self.logical_shape)}, int{self.bits}, "
+                f"{self.group_mode}, sink={self.sink_tokens}, {gb:.3f} GB)")
+
+
+def _materialize_args(x):
+    if isinstance(x, QuantKVWindow):
+        return x.materialize()
+    if isinstance(x, (list, tuple)):
+        return type(x)(_materialize_args(y) for y in x)
+    if isinstance(x, dict):
+        return {k: _materialize_args(v) for k, v in x.items()}
+    return x
+
+
+class QuantKVWindow:
+    """Lazy [B, hi-lo, H, D] bf16 view of tokens [lo, hi) of a QuantKVTensor.
+
+    attention() consumes it packed. Everything else sees the dequantized bf16
+    window of the reference's __getitem__ (quant_kv.py:189-199), materialized on
+    use: torch functions (via __torch_function__), tensor methods and
+    attributes (delegated), arithmetic operators and `.clone()`.
+    """
+
+    def __init__(self, cache: QuantKVTensor, lo: int, hi: int):
+        self.cache, self.lo, self.hi = cache, lo, hi
+
+    @property
+    def shape(self):
+        c = self.cache
+        return torch.Size((c.n_streams, self.hi - self.lo, c.n_heads, c.head_dim))
+
+    @property
+    def dtype(self):
+        return self.cache.dtype
+
+    @property
+    def device(self):
+        return self.cache.device
+
+    def size(self, dim=None):
+        return self.shape if dim is None else self.shape[dim]
+
+    def dim(self):
+        return 4
+
+    def materialize(self) -> torch.Tensor:
+        return self.cache.read(self.lo, self.hi)
+
+    def clone(self, *a, **kw):
+        # the runtime's eviction `kv[:, a:b] = kv[:, c:d].clone()` (quant_kv.py:13): the
+        # reference dequantizes here and requantizes on the write (quant_kv.py:217-218)
+        return self.materialize()
+
+    @classmethod
+    def __torch_function__(cls, func, types, args=(), kwargs=None):
+        return func(*_materialize_args(args), **_materialize_args(kwargs or {}))
+
+    def __getattr__(self, name):
+        if name.startswith("__"):
+            raise AttributeError(name)
+        return getattr(self.materialize(), name)
+
+    def __getitem__(self, idx):
+        return self.materialize()[idx]
+
+    def __len__(self):
+        return self.cache.n_streams
+
+    def __array__(self, dtype=None):
+        return np.asarray(self.materialize().float().cpu(), dtype=dtype)
+
+    def __repr__(self):
+        return f"QuantKVWindow({self.cache!r}, tokens [{self.lo}, {self.hi}))"
+
+
+def _binop(name):
+    def f(self, other):
+        return getattr(self.materialize(), name)(_materialize_args(other))
+    f.__name__ = name
+    return f
+
+
+for _n in ("__add__", "__radd__", "__sub__", "__rsub__", "__mul__", "__rmul__", "__truediv__",
+           "__rtruediv__", "__matmul__", "__rmatmul__", "__eq__", "__ne__", "__lt__", "__le__",
+           "__gt__", "__ge__"):
+    setattr(QuantKVWindow, _n, _binop(_n))
+for _n in ("__neg__", "__abs__", "__float__"):
+    setattr(QuantKVWindow, _n, (lambda nm: lambda self: getattr(self.materialize(), nm)())(_n))
+QuantKVWindow.__hash__ = object.__hash__
+
+
+def install(pipeline, k_bits=4, v_bits=4, group_mode="bands", sink_frames=0, verbose=True):
+    """Swaps the kv_cache1 allocation for QuantKVTensor (quant_kv.py:228-269).
+
+    Patches the instance's `_initialize_kv_cache`; the cross-attention cache is
+    not touched. Returns the original method.
+    """
+    sink_tokens = sink_frames * FRAME_SEQ_LEN
+    orig = pipeline._initialize_kv_cache
+
+    def _initialize_kv_cache(batch_size, dtype, device):
+        if pipeline.local_attn_size != -1:
+            size = pipeline.local_attn_size * pipeline.frame_seq_length
+        else:
+            size = 32760
+        cfg = pipeline.generator.model.config
+        shape = [batch_size, size, cfg.num_heads, cfg.dim // cfg.num_heads]
+        existing = getattr(pipeline, "kv_cache1", None)
+        if existing and isinstance(existing[0]["k"], QuantKVTensor) \
+                and list(existing[0]["k"].shape) == shape:
+            for e in existing:
+                e["k"].zero_()
+                e["v"].zero_()
+                e["global_end_index"] = 0
+                e["local_end_index"] = 0
+            return
+        cache = []
+        for _ in range(pipeline.num_transformer_blocks):
+            cache.append({
+                "k": QuantKVTensor(shape, device, dtype, k_bits, group_mode, sink_tokens),
+                "v": QuantKVTensor(shape, device, dtype, v_bits, group_mode, sink_tokens),
+                "global_end_index": 0,
+                "local_end_index": 0,
+            })
+        pipeline.k_shape = shape
+        pipeline.v_shape = shape
+        pipeline.kv_cache1 = cache
+        if verbose:
+            tot = sum(e["k"].storage_bytes() + e["v"].storage_bytes() for e in cache)
+            bf16 = 2 * len(cache) * shape[0] * shape[1] * shape[2] * shape[3] * 2
+            print(f"QuantKVCache: {cache[0]['k']}  |  {len(cache)} layers  "
+                  f"{tot / 1e9:.3f} GB vs {bf16 / 1e9:.3f} GB bf16  "
+                  f"(frees {(bf16 - tot) / 1e9:.3f} GB)", flush=True)
+
+    pipeline._initialize_kv_cache = _initialize_kv_cache
+    return orig
