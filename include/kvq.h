@@ -91,6 +91,38 @@ KVQ_API int kvq_dequantize(const void* codes, const void* scales, const void* si
                    int64_t n_tokens, int n_heads, int head_dim,
                    const int32_t* chan_band, int n_groups, int bits, void* stream);
 
+/*
+ * Fused int4-KV attention over a cache window, reading K and V packed.
+ * Replaces the read path `attention(q, kv_cache["k"][:, lo:hi], kv_cache["v"][:, lo:hi])`
+ * (quant_kv.py:14): QuantKVTensor.__getitem__'s dequantize + bf16 sink overlay
+ * (quant_kv.py:189-199) followed by the upstream attention() call that
+ * probe_attention.py:97-124 hooks (softmax(q k^T / sqrt(D)) v, non-causal).
+ *
+ *   q          bf16 [batch][n_q][n_heads][head_dim], token stride q_token_stride
+ *   k_*, v_*   cache storage of K and V as written by kvq_quantize, streams
+ *              stacked: stream b owns cache rows [b*cache_tokens, (b+1)*cache_tokens)
+ *              and sink rows [b*sink_tokens, (b+1)*sink_tokens)
+ *   lo, hi     window of cache tokens; tokens < sink_tokens come from the sinks
+ *   out        bf16 [batch][n_q][n_heads][head_dim], token stride out_token_stride
+ *   softmax_scale  <= 0 selects 1/sqrt(head_dim)
+ * head_dim 128, int4 K and V, and the five reference group layouts.
+ */
+KVQ_API int kvq_attention(const void* q, int64_t q_token_stride,
+                          const void* k_codes, const void* k_scales, const void* k_sink,
+                          const void* v_codes, const void* v_scales, const void* v_sink,
+                          int64_t cache_tokens, int64_t sink_tokens, int64_t lo, int64_t hi,
+                          void* out, int64_t out_token_stride, int batch, int64_t n_q,
+                          int n_heads, int head_dim, const int32_t* chan_band, int n_groups,
+                          int k_bits, int v_bits, float softmax_scale, void* stream);
+
+/*
+ * Synchronizes the current device and returns the library's device status word:
+ * 0 = no kernel gave up, 1 = a kernel's bounded wait timed out (its output is
+ * invalid). reset != 0 clears it. No counterpart in the reference (its Triton
+ * kernels have no waits).
+ */
+KVQ_API int kvq_device_status(int reset);
+
 #ifdef __cplusplus
 }
 #endif

@@ -116,3 +116,44 @@ def dequantize_into(codes: torch.Tensor, scales: torch.Tensor, out: torch.Tensor
             _stream(dev))
     _lib.check(rc, "kvq_dequantize")
     return out
+
+
+def attention_packed(q: torch.Tensor, k_cache, v_cache, lo: int, hi: int, out: torch.Tensor | None = None,
+                     softmax_scale: float | None = None) -> torch.Tensor:
+    """Fused int4-KV attention of q [B, Lq, H, D] bf16 over tokens [lo, hi) of two
+    QuantKVTensor caches (same shape, group mode and sink). Returns out [B, Lq, H, D] bf16."""
+    dev = _require_cuda(q, k_cache.packed, v_cache.packed, out)
+    if q.dtype != torch.bfloat16 or q.dim() != 4:
+        raise TypeError("q must be a [B, Lq, H, D] bfloat16 tensor")
+    B, Lq, H, D = q.shape
+    for c in (k_cache, v_cache):
+        if (c.n_streams, c.n_heads, c.head_dim) != (B, H, D):
+            raise ValueError(f"cache shape {tuple(c.shape)} does not match q {tuple(q.shape)}")
+    if (k_cache.n_tokens, k_cache.sink_tokens, k_cache.bands) != (v_cache.n_tokens, v_cache.sink_tokens,
+                                                                  v_cache.bands):
+        raise ValueError("K and V caches must share tokens, sink and group mode")
+    if q.stride(3) != 1 or q.stride(2) != D or q.stride(0) != Lq * q.stride(1):
+        q = q.contiguous()
+    if out is None:
+        out = torch.empty((B, Lq, H, D), dtype=torch.bfloat16, device=dev)
+    elif (out.dtype != torch.bfloat16 or tuple(out.shape) != (B, Lq, H, D) or out.stride(3) != 1
+          or out.stride(2) != D or out.stride(0) != Lq * out.stride(1)):
+        raise ValueError("out must be bf16 [B, Lq, H, D] with contiguous heads and a uniform token stride")
+    cb = _host_map(k_cache.chan_band_host)
+    with torch.cuda.device(dev):
+        rc = _lib.load().kvq_attention(
+            _ptr(q), q.stride(1), _ptr(k_cache.packed), _ptr(k_cache.scales), _ptr(k_cache.sink),
+            _ptr(v_cache.packed), _ptr(v_cache.scales), _ptr(v_cache.sink), k_cache.n_tokens,
+            k_cache.sink_tokens if k_cache.sink is not None else 0, int(lo), int(hi), _ptr(out), out.stride(1),
+            B, Lq, H, D, cb.ctypes.data_as(ctypes.c_void_p), len(k_cache.bands), k_cache.bits, v_cache.bits,
+            float(softmax_scale) if softmax_scale else 0.0, _stream(dev))
+    _lib.check(rc, "kvq_attention")
+    return out
+
+
+def device_status(reset: bool = True) -> int:
+    """Synchronizes and returns the library's device status word (0 = ok)."""
+    rc = _lib.load().kvq_device_status(1 if reset else 0)
+    if rc < 0:
+        _lib.check(rc, "kvq_device_status")
+    return rc

@@ -1,0 +1,47 @@
+"""Head-parallel sharding of the int4-KV attention across GPUs.
+
+The 40 heads are split in contiguous ranges over the ranks (40/20/10/5 per GPU
+on 1/2/4/8 B200s); each rank holds the cache of its heads only and runs the
+attention for them on all streams; one NCCL all-gather over NVLink collects the
+attention outputs. The reference is single-GPU throughout, so this module has no
+counterpart there.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+
+def head_range(n_heads: int, world: int, rank: int) -> tuple[int, int]:
+    """Contiguous, balanced head range [h0, h1) of `rank`."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"bad rank {rank} of {world}")
+    if n_heads < world:
+        raise ValueError(f"{n_heads} heads cannot be split over {world} ranks")
+    base, extra = divmod(n_heads, world)
+    h0 = rank * base + min(rank, extra)
+    return h0, h0 + base + (1 if rank < extra else 0)
+
+
+def gather_buffer(local_out: torch.Tensor, world: int) -> torch.Tensor:
+    """Receive buffer [world, *local_out.shape] for gather_outputs()."""
+    return torch.empty((world, *local_out.shape), dtype=local_out.dtype, device=local_out.device)
+
+
+def gather_outputs(local_out: torch.Tensor, buf: torch.Tensor | None = None, group=None) -> torch.Tensor:
+    """All-gathers per-rank outputs [B, Lq, Hl, D] into [world, B, Lq, Hl, D].
+
+    Equal head counts per rank are required (all_gather_into_tensor). The
+    result is rank-major: rank r's heads are head_range(H, world, r).
+    """
+    world = dist.get_world_size(group)
+    if buf is None:
+        buf = gather_buffer(local_out, world)
+    dist.all_gather_into_tensor(buf, local_out.contiguous(), group=group)
+    return buf
+
+
+def assemble_heads(gathered: torch.Tensor) -> torch.Tensor:
+    """[world, B, Lq, Hl, D] -> [B, Lq, world*Hl, D] in global head order."""
+    w, B, Lq, Hl, D = gathered.shape
+    return gathered.permute(1, 2, 0, 3, 4).reshape(B, Lq, w * Hl, D)

@@ -357,3 +357,24 @@ def install(pipeline, k_bits=4, v_bits=4, group_mode="bands", sink_frames=0, ver
 
     pipeline._initialize_kv_cache = _initialize_kv_cache
     return orig
+
+
+def attention(q, k, v, *args, softmax_scale=None, out=None, **kwargs):
+    """Attention over a cache read, consuming the packed window directly.
+
+    The runtime's read path `attention(q, kv_cache["k"][:, lo:hi],
+    kv_cache["v"][:, lo:hi])` (quant_kv.py:14) with q [B, Lq, H, D] bf16 and k, v
+    QuantKVWindow views of the same token range. Non-causal softmax(q k^T *
+    scale) v, scale 1/sqrt(D) by default, bf16 output [B, Lq, H, D]. Plain
+    tensors for k or v raise TypeError: this build has no non-packed path.
+    Extra positional/keyword arguments of the upstream signature other than
+    softmax_scale are not supported and raise.
+    """
+    if not isinstance(k, QuantKVWindow) or not isinstance(v, QuantKVWindow):
+        raise TypeError("attention() takes k and v as QuantKVTensor windows (t[:, lo:hi]); "
+                        "plain tensors have no packed form")
+    if (k.lo, k.hi) != (v.lo, v.hi):
+        raise ValueError(f"k window [{k.lo},{k.hi}) and v window [{v.lo},{v.hi}) differ")
+    if args or kwargs:
+        raise TypeError(f"unsupported attention arguments: {args} {sorted(kwargs)}")
+    return _ops.attention_packed(q, k.cache, v.cache, k.lo, k.hi, out=out, softmax_scale=softmax_scale)
