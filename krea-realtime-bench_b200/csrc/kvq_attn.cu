@@ -178,7 +178,7 @@ __device__ __forceinline__ float ex2(float x) {
 }
 
 template <class L>
-__global__ void __maxnreg__(224) attention_kernel(const __grid_constant__ Args a) {
+__global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_constant__ Args a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
@@ -257,23 +257,21 @@ __global__ void __maxnreg__(224) attention_kernel(const __grid_constant__ Args a
       const int buf = j & 1;
       if (!mbar_wait_warp(&bars[kSFull0 + buf], (j >> 1) & 1, abort, &g_attn_status)) { ok = false; break; }
       tc_fence_after();
-      uint32_t s[128];
-#pragma unroll
-      for (int k = 0; k < 4; ++k)
-        tmem_ld32(lane_base + kColS + buf * 128 + 32 * k, reinterpret_cast<uint32_t(&)[32]>(s[32 * k]));
-      tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(&bars[kSEmpty0 + buf]);
-
+      const uint32_t sb = lane_base + kColS + buf * 128;
       const int valid = min(BN, a.Lk - j * BN);
+      // pass 1: row max of S (64 columns per TMEM round trip)
       float mx = -INFINITY;
-      if (valid == BN) {
 #pragma unroll
-        for (int c = 0; c < 128; ++c) mx = fmaxf(mx, __uint_as_float(s[c]));
-      } else {
+      for (int k = 0; k < 2; ++k) {
+        uint32_t s0[32], s1[32];
+        tmem_ld32(sb + 64 * k, s0);
+        tmem_ld32(sb + 64 * k + 32, s1);
+        tmem_wait_ld();
 #pragma unroll
-        for (int c = 0; c < 128; ++c)
-          if (c < valid) mx = fmaxf(mx, __uint_as_float(s[c]));
+        for (int c = 0; c < 32; ++c) {
+          if (64 * k + c < valid) mx = fmaxf(mx, __uint_as_float(s0[c]));
+          if (64 * k + 32 + c < valid) mx = fmaxf(mx, __uint_as_float(s1[c]));
+        }
       }
       const float mt = mx * a.scale_log2;
       // P_j goes to the single P buffer and O may be rescaled: PV_{j-1} must be done
@@ -301,21 +299,33 @@ __global__ void __maxnreg__(224) attention_kernel(const __grid_constant__ Args a
         }
         tmem_wait_st();
       }
+      // pass 2: P = exp2(S * scale_log2 - m), bf16 into the swizzled P tile
       const float nm = -m;
       float sum = 0.0f;
 #pragma unroll
-      for (int c8 = 0; c8 < 16; ++c8) {
-        float p[8];
+      for (int k = 0; k < 2; ++k) {
+        uint32_t s0[32], s1[32];
+        tmem_ld32(sb + 64 * k, s0);
+        tmem_ld32(sb + 64 * k + 32, s1);
+        tmem_wait_ld();
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const int c = 8 * c8 + k;
-          float e = ex2(fmaf(__uint_as_float(s[c]), a.scale_log2, nm));
-          p[k] = (c < valid) ? e : 0.0f;
-          sum += p[k];
+        for (int c8 = 0; c8 < 8; ++c8) {
+          float p[8];
+#pragma unroll
+          for (int t = 0; t < 8; ++t) {
+            const int cc = 8 * c8 + t;  // column within this 64-column half
+            const float sv = __uint_as_float(cc < 32 ? s0[cc] : s1[cc - 32]);
+            const float e = ex2(fmaf(sv, a.scale_log2, nm));
+            p[t] = (64 * k + cc < valid) ? e : 0.0f;
+            sum += p[t];
+          }
+          st_shared_v4(pb + tile_off(r, 8 * k + c8),
+                       make_uint4(pack_bf16x2(p[0], p[1]), pack_bf16x2(p[2], p[3]), pack_bf16x2(p[4], p[5]),
+                                  pack_bf16x2(p[6], p[7])));
         }
-        st_shared_v4(pb + tile_off(r, c8), make_uint4(pack_bf16x2(p[0], p[1]), pack_bf16x2(p[2], p[3]),
-                                                      pack_bf16x2(p[4], p[5]), pack_bf16x2(p[6], p[7])));
       }
+      tc_fence_before();
+      mbar_arrive(&bars[kSEmpty0 + buf]);
       l += sum;
       fence_proxy_async_smem();
       tc_fence_before();
