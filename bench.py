@@ -497,6 +497,36 @@ def run_extras(dev, peaks):
     return res
 
 
+def run_profile_case(case: str, launches: int = 6):
+    """A small single-GPU case for ncu captures: a few launches of one kernel on
+    inputs larger than L2, nothing else."""
+    import quant_kv
+    import quant_kv_kernels
+    from kvq import ops, synth
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    if case == "attention":
+        tk, tv, _, _ = make_caches(1, LK, H_TOTAL, SINK, dev, seed=1)
+        q = synth.make_q(1, LQ, H_TOTAL, seed=2, device=dev)
+        out = torch.empty_like(q)
+        for _ in range(launches):
+            ops.attention_packed(q, tk, tv, 0, LK, out=out)
+    else:
+        bands = quant_kv._band_edges(D, MODE)
+        G = len(bands)
+        cb = quant_kv_kernels.host_chan_band(quant_kv_kernels.build_chan_band(bands, D, "cpu"))
+        L = 21 * FRAME
+        x = synth.make_k(L, H_TOTAL, seed=3, device=dev)
+        codes = torch.empty((L, H_TOTAL, D // 2), dtype=torch.uint8, device=dev)
+        scales = torch.empty((L, H_TOTAL, G), dtype=torch.bfloat16, device=dev)
+        for _ in range(launches):
+            ops.quantize_into(x, codes, scales, cb, G, 4)
+            if case == "dequantize":
+                ops.dequantize_into(codes, scales, x, cb, G, 4)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_case": case, "launches": launches, "status": ops.device_status()}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -506,7 +536,12 @@ def main():
     ap.add_argument("--no-extras", action="store_true", help="skip quantize / prefill extras")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--profile-case", choices=("attention", "quantize", "dequantize"),
+                    help="run a few launches of one kernel for an ncu capture and exit")
     args = ap.parse_args()
+    if args.profile_case:
+        run_profile_case(args.profile_case)
+        return
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
