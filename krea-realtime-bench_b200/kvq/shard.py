@@ -24,8 +24,10 @@ def head_range(n_heads: int, world: int, rank: int) -> tuple[int, int]:
 
 
 def gather_buffer(local_out: torch.Tensor, world: int) -> torch.Tensor:
-    """Receive buffer [world, *local_out.shape] for gather_outputs()."""
-    return torch.empty((world, *local_out.shape), dtype=local_out.dtype, device=local_out.device)
+    """Receive buffer for gather_outputs(): [world * B, Lq, Hl, D], i.e. the
+    per-rank outputs concatenated along the first dimension."""
+    return torch.empty((world * local_out.shape[0], *local_out.shape[1:]), dtype=local_out.dtype,
+                       device=local_out.device)
 
 
 def gather_outputs(local_out: torch.Tensor, buf: torch.Tensor | None = None, group=None) -> torch.Tensor:
@@ -38,7 +40,7 @@ def gather_outputs(local_out: torch.Tensor, buf: torch.Tensor | None = None, gro
     if buf is None:
         buf = gather_buffer(local_out, world)
     dist.all_gather_into_tensor(buf, local_out.contiguous(), group=group)
-    return buf
+    return buf.view(world, *local_out.shape)
 
 
 def assemble_heads(gathered: torch.Tensor) -> torch.Tensor:
