@@ -1,26 +1,38 @@
-// Fused int4-KV attention for sm_100a (tcgen05 tensor cores, TMEM accumulators).
+// Fused int4-KV attention for sm_100a (tcgen05 tensor cores, TMEM, TMA).
 //
 // Computes, per (stream b, head h), O = softmax(Q K^T * scale) V over the cache
-// window [lo, hi), reading K and V in packed form: the reference dequantizes the
+// window [lo, hi), reading K and V in packed form. The reference dequantizes the
 // window to bf16 (QuantKVTensor.__getitem__, quant_kv.py:189-199) and hands it to
-// the upstream attention() (hooked at probe_attention.py:102-124). Tokens below
-// sink_tokens are read from the exact bf16 sink copy, as the reference's read
-// overlays them (quant_kv.py:196-198). The dequantized values are bit-identical
-// to the reference's (fp32 q * scale, rounded to bf16).
+// the upstream attention() (hooked at probe_attention.py:102-124); tokens below
+// sink_tokens come from the exact bf16 sink copy, as the reference's read
+// overlays them (quant_kv.py:196-198).
 //
-// One CTA per (128-row Q tile, head, stream); 288 threads, warp-specialised:
-//   warps 0-3  converters: load Q once; per KV tile of 128 tokens load codes and
-//              scales (or sink rows), dequantize to bf16 and store K and V into
-//              double-buffered, 128B-swizzled shared-memory tiles;
-//   warps 4-7  softmax: thread r owns Q row r (= TMEM lane r); reads S from TMEM,
-//              online softmax in base 2 with lazy rescaling (O is rescaled only
-//              when the running max grows by more than 2^8), writes P (bf16) to
-//              shared memory, finally normalises O and stores it;
-//   warp 8     TMEM allocation and the single thread that issues tcgen05.mma:
-//              S_j = Q K_j^T (M=128, N=128, K=128) into one of two TMEM buffers,
-//              O += P_j V_j (M=128, N=128, K=128) into the TMEM O accumulator.
-// Synchronisation is by mbarriers; every wait gives up after about a second,
-// raising a device status word read back by kvq_device_status().
+// One CTA per (pair of 128-row Q tiles, head, stream); the two Q tiles share
+// every dequantized K/V tile. 512 threads, warp-specialised:
+//   warps 0-3 / 4-7  softmax for Q tile 0 / 1: thread r owns Q row r (TMEM lane
+//                    r). Loads its Q row into TMEM once; per KV tile reads S
+//                    (64 columns) from TMEM, online base-2 softmax with lazy
+//                    rescaling of O (only when the row max grows by > 2^8),
+//                    writes P as bf16 back into TMEM over S; finally normalises O.
+//   warps 8-11       converters: per KV tile of 64 tokens, warps 8-9 dequantize
+//                    the K rows and 10-11 the V rows (one row per thread) from
+//                    the TMA-staged codes into 128B-swizzled bf16 tiles, with
+//                    packed bf16x2 arithmetic (bit-identical to the reference).
+//   warp 12          TMA producer: packed codes (SWIZZLE_64B staging) and, for
+//                    tiles that reach into the sink, the bf16 sink rows straight
+//                    into the bf16 tiles (SWIZZLE_128B, the MMA's layout).
+//   warp 13          TMEM allocation (512 columns) and the thread issuing
+//                    tcgen05.mma with A in TMEM: S_x = Q_x K^T (M=128, N=64,
+//                    K=128) and O_x += P_x V (M=128, N=128, K=64), V read as an
+//                    MN-major shared-memory operand.
+// TMEM columns: Q_0 [0,64) Q_1 [64,128) (bf16 pairs), O_0 [128,256) O_1
+// [256,384), S_0 [384,448) S_1 [448,512) (P_x over the first 32 of S_x).
+// Synchronisation is by mbarriers with one arrival per warp; every wait gives up
+// after about a second, raising the device status word (kvq_device_status()).
+#include <cuda.h>
+#include <cuda_bf16.h>
+
+#include <cstring>
 #include <utility>
 
 #include "kvq_common.cuh"
@@ -33,53 +45,59 @@ __device__ int g_attn_status = 0;
 
 namespace attn {
 
-constexpr int BM = 128, BN = 128, D = 128;
-constexpr int kConvThreads = 128, kSoftThreads = 128;
-constexpr int kThreads = kConvThreads + kSoftThreads + 32;
-constexpr int kMmaWarp = 8;
+constexpr int BM = 128;   // rows per Q tile
+constexpr int BN = 64;    // KV tokens per tile
+constexpr int D = 128;
+constexpr int NS_KV = 3;  // bf16 K/V tile stages
+constexpr int NS_LD = 4;  // packed-code stages
+constexpr int kThreads = 16 * 32;
+constexpr int kConvWarp0 = 8, kProdWarp = 12, kMmaWarp = 13;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS = 0;    // S buffers at columns 0 and 128
-constexpr uint32_t kColO = 256;  // O accumulator
+constexpr uint32_t kColQ = 0, kColO = 128, kColS = 384;
 
-// shared memory map (bytes from a 1024-aligned base)
-constexpr int kTile = BM * D * 2;  // 32 KB bf16 tile, two 16 KB swizzle atoms
-constexpr int kOffQ = 0;
-constexpr int kOffK = kOffQ + kTile;       // 2 buffers
-constexpr int kOffV = kOffK + 2 * kTile;   // 2 buffers
-constexpr int kOffP = kOffV + 2 * kTile;
-constexpr int kOffBar = kOffP + kTile;
-constexpr int kNumBars = 12;
+constexpr int kKVTile = BN * D * 2;     // 16 KB: two 8 KB SWIZZLE_128B atoms (d 0-63, 64-127)
+constexpr int kAtom = BN * 128;         // 8 KB
+constexpr int kCodeTile = BN * 64;      // 4 KB: 64 tokens x 64 B, SWIZZLE_64B
+constexpr int kOffK = 0;
+constexpr int kOffV = kOffK + NS_KV * kKVTile;
+constexpr int kOffKC = kOffV + NS_KV * kKVTile;
+constexpr int kOffVC = kOffKC + NS_LD * kCodeTile;
+constexpr int kOffBar = kOffVC + NS_LD * kCodeTile;
+// barrier indices
+constexpr int bLdFull = 0, bLdEmpty = bLdFull + NS_LD, bKvFull = bLdEmpty + NS_LD, bKvEmpty = bKvFull + NS_KV,
+              bQReady = bKvEmpty + NS_KV, bSFull = bQReady + 2, bPFull = bSFull + 2, bOFinal = bPFull + 2,
+              bMmaDone = bOFinal + 2, kNumBars = bMmaDone + 1;
 constexpr int kOffMisc = kOffBar + kNumBars * 8;
 constexpr int kSmemBytes = kOffMisc + 64 + 1024;  // + alignment slack
 
-enum Bar { kQFull = 0, kKVFull0 = 1, kKVEmpty0 = 3, kSFull0 = 5, kSEmpty0 = 7, kPFull = 9, kPVDone = 10, kFinal = 11 };
-
-struct Args {
+struct alignas(64) Args {
+  CUtensorMap tm_kc, tm_vc;  // codes [B*S rows, H*64 B], box 64 x 64, SWIZZLE_64B
+  CUtensorMap tm_ks, tm_vs;  // sinks [B*sink rows, H*128 bf16], box 64 x 64, SWIZZLE_128B
   const uint16_t* q;
   int64_t q_tok_stride, q_batch_stride;
-  const uint8_t* kc;
   const uint16_t* ks;
-  const uint16_t* ksink;
-  const uint8_t* vc;
   const uint16_t* vs;
-  const uint16_t* vsink;
   int64_t cache_tokens, sink_tokens, lo;
-  int Lk, Lq, H, G;
+  int Lk, Lq, H;
   uint16_t* out;
   int64_t o_tok_stride, o_batch_stride;
   float scale_log2;
-  GroupMap map;
 };
 
-// byte offset of 16-byte chunk c (8 bf16 columns) of row r in a 128x128 bf16 tile
-// stored as two K-major SWIZZLE_128B atoms (columns 0-63 and 64-127).
+// byte offset of 16-byte chunk c (8 bf16 columns) of row r in a 64 x 128 bf16
+// tile stored as two K-major SWIZZLE_128B atoms (columns 0-63 and 64-127).
 __device__ __forceinline__ uint32_t tile_off(int r, int c) {
-  return static_cast<uint32_t>((c >> 3) * (BM * 128) + r * 128 + (((c & 7) ^ (r & 7)) << 4));
+  return static_cast<uint32_t>((c >> 3) * kAtom + r * 128 + (((c & 7) ^ (r & 7)) << 4));
 }
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
   asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
                : "memory");
+}
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+  return v;
 }
 
 template <class L>
@@ -89,86 +107,81 @@ __host__ __device__ constexpr int group_of(int ch) {
   return g;
 }
 
-// 8 channels (one 32-bit word of nibbles) -> 8 bf16, bit-identical to the
-// reference dequant: bf16(float(code - 8) * float(scale)).
+__device__ __forceinline__ uint32_t bf2_sub(uint32_t a, uint32_t b) {
+  __nv_bfloat162 r = __hsub2(*reinterpret_cast<__nv_bfloat162*>(&a), *reinterpret_cast<__nv_bfloat162*>(&b));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+__device__ __forceinline__ uint32_t bf2_mul(uint32_t a, uint32_t b) {
+  __nv_bfloat162 r = __hmul2(*reinterpret_cast<__nv_bfloat162*>(&a), *reinterpret_cast<__nv_bfloat162*>(&b));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+
+// Channels 8C..8C+7 (one 32-bit word of nibbles, w; ws = w >> 4) -> 8 bf16.
+// Pair i = channels (8C+2i, 8C+2i+1) = byte i: bf16x2 (128 + lo, 128 + hi) by a
+// byte permute and one mask/or, minus 136 (exact), times (s_g, s_g): the exact
+// product rounded to bf16, i.e. the reference's bf16(float(q) * float(scale)).
 template <class L, int C>
-__device__ __forceinline__ uint4 deq_chunk(uint32_t w, const float (&sf)[L::G]) {
-  constexpr int g0 = group_of<L>(8 * C + 0), g1 = group_of<L>(8 * C + 1), g2 = group_of<L>(8 * C + 2),
-                g3 = group_of<L>(8 * C + 3), g4 = group_of<L>(8 * C + 4), g5 = group_of<L>(8 * C + 5),
-                g6 = group_of<L>(8 * C + 6), g7 = group_of<L>(8 * C + 7);
-  auto q = [&](int k) { return static_cast<float>(static_cast<int>((w >> (4 * k)) & 0xFu) - 8); };
-  return make_uint4(pack_bf16x2(__fmul_rn(q(0), sf[g0]), __fmul_rn(q(1), sf[g1])),
-                    pack_bf16x2(__fmul_rn(q(2), sf[g2]), __fmul_rn(q(3), sf[g3])),
-                    pack_bf16x2(__fmul_rn(q(4), sf[g4]), __fmul_rn(q(5), sf[g5])),
-                    pack_bf16x2(__fmul_rn(q(6), sf[g6]), __fmul_rn(q(7), sf[g7])));
+__device__ __forceinline__ uint4 deq8(uint32_t w, uint32_t ws, const uint32_t (&sp)[L::G]) {
+  constexpr uint32_t k136 = 0x43084308u;  // bf16x2 (136, 136)
+  uint32_t o[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint32_t t = __byte_perm(w, ws, static_cast<uint32_t>(((4 + i) << 8) | i));
+    t = (t & 0x000F000Fu) | 0x43004300u;
+    o[i] = t;
+  }
+  constexpr int g0 = group_of<L>(8 * C + 0), g1 = group_of<L>(8 * C + 2), g2 = group_of<L>(8 * C + 4),
+                g3 = group_of<L>(8 * C + 6);
+  return make_uint4(bf2_mul(bf2_sub(o[0], k136), sp[g0]), bf2_mul(bf2_sub(o[1], k136), sp[g1]),
+                    bf2_mul(bf2_sub(o[2], k136), sp[g2]), bf2_mul(bf2_sub(o[3], k136), sp[g3]));
 }
 
 template <class L, int... Cs>
-__device__ __forceinline__ void deq_row_store(const uint32_t (&w)[16], const float (&sf)[L::G], uint32_t row_base,
-                                              int r, std::integer_sequence<int, Cs...>) {
-  (st_shared_v4(row_base + tile_off(r, Cs), deq_chunk<L, Cs>(w[Cs], sf)), ...);
+__device__ __forceinline__ void deq_row(const uint32_t (&w)[16], const uint32_t (&sp)[L::G], uint32_t dst, int r,
+                                        std::integer_sequence<int, Cs...>) {
+  (st_shared_v4(dst + tile_off(r, Cs), deq8<L, Cs>(w[Cs], w[Cs] >> 4, sp)), ...);
 }
 
+// Raw scale words of one row (bf16 pairs, or single bf16 values for odd G).
 template <class L>
-__device__ __forceinline__ void load_scales(const uint16_t* p, float (&sf)[L::G]) {
+struct ScaleWords {
+  static constexpr int N = (L::G * 2) % 4 == 0 ? L::G / 2 : L::G;
+  uint32_t v[N];
+};
+
+template <class L>
+__device__ __forceinline__ void load_scale_words(const uint16_t* p, ScaleWords<L>& s) {
   constexpr int G = L::G;
   if constexpr ((G * 2) % 8 == 0) {
 #pragma unroll
     for (int i = 0; i < G / 4; ++i) {
-      uint2 v = *reinterpret_cast<const uint2*>(p + 4 * i);
-      sf[4 * i + 0] = bf16lo_to_f32(v.x);
-      sf[4 * i + 1] = bf16hi_to_f32(v.x);
-      sf[4 * i + 2] = bf16lo_to_f32(v.y);
-      sf[4 * i + 3] = bf16hi_to_f32(v.y);
+      uint2 v = __ldg(reinterpret_cast<const uint2*>(p + 4 * i));
+      s.v[2 * i] = v.x;
+      s.v[2 * i + 1] = v.y;
     }
   } else if constexpr ((G * 2) % 4 == 0) {
 #pragma unroll
-    for (int i = 0; i < G / 2; ++i) {
-      uint32_t v = *reinterpret_cast<const uint32_t*>(p + 2 * i);
-      sf[2 * i + 0] = bf16lo_to_f32(v);
-      sf[2 * i + 1] = bf16hi_to_f32(v);
-    }
+    for (int i = 0; i < G / 2; ++i) s.v[i] = __ldg(reinterpret_cast<const uint32_t*>(p + 2 * i));
   } else {
 #pragma unroll
-    for (int i = 0; i < G; ++i) sf[i] = bf16_bits_to_f32(p[i]);
+    for (int i = 0; i < G; ++i) s.v[i] = __ldg(p + i);
   }
 }
 
-// Writes row r (one token of one head) of a K or V tile: zeros past the window,
-// the exact bf16 sink copy below sink_tokens, else the dequantized codes.
+// (s_g, s_g) bf16x2 per group
 template <class L>
-__device__ __forceinline__ void convert_row(const Args& a, const uint8_t* codes, const uint16_t* scales,
-                                            const uint16_t* sink, int b, int h, int jt, uint32_t tile_base,
-                                            int r) {
-  if (jt >= a.Lk) {
+__device__ __forceinline__ void scale_pairs(const ScaleWords<L>& s, uint32_t (&sp)[L::G]) {
+  constexpr int G = L::G;
+  if constexpr ((G * 2) % 4 == 0) {
 #pragma unroll
-    for (int c = 0; c < 16; ++c) st_shared_v4(tile_base + tile_off(r, c), make_uint4(0, 0, 0, 0));
-    return;
+    for (int i = 0; i < G / 2; ++i) {
+      sp[2 * i] = __byte_perm(s.v[i], 0, 0x1010);
+      sp[2 * i + 1] = __byte_perm(s.v[i], 0, 0x3232);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < G; ++i) sp[i] = __byte_perm(s.v[i], 0, 0x1010);
   }
-  const int64_t tok = a.lo + jt;
-  if (tok < a.sink_tokens) {
-    const uint16_t* src = sink + ((static_cast<int64_t>(b) * a.sink_tokens + tok) * a.H + h) * D;
-    uint4 v[16];
-#pragma unroll
-    for (int c = 0; c < 16; ++c) v[c] = ld_global_nc_v4(src + 8 * c);
-#pragma unroll
-    for (int c = 0; c < 16; ++c) st_shared_v4(tile_base + tile_off(r, c), v[c]);
-    return;
-  }
-  const int64_t row = (static_cast<int64_t>(b) * a.cache_tokens + tok) * a.H + h;
-  const uint4* cp = reinterpret_cast<const uint4*>(codes + row * (D / 2));
-  uint32_t w[16];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    uint4 v = ld_global_nc_v4(cp + i);
-    w[4 * i + 0] = v.x;
-    w[4 * i + 1] = v.y;
-    w[4 * i + 2] = v.z;
-    w[4 * i + 3] = v.w;
-  }
-  float sf[L::G];
-  load_scales<L>(scales + row * L::G, sf);
-  deq_row_store<L>(w, sf, tile_base, r, std::make_integer_sequence<int, 16>{});
 }
 
 __device__ __forceinline__ float ex2(float x) {
@@ -188,22 +201,27 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
-  const int q0 = blockIdx.x * BM;
+  const int q0 = blockIdx.x * (2 * BM);
   const int h = blockIdx.y;
   const int b = blockIdx.z;
   const int nkv = (a.Lk + BN - 1) / BN;
 
   if (tid == 0) {
-    mbar_init(&bars[kQFull], kConvThreads);
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&bars[kKVFull0 + i], kConvThreads);
-      mbar_init(&bars[kKVEmpty0 + i], 1);
-      mbar_init(&bars[kSFull0 + i], 1);
-      mbar_init(&bars[kSEmpty0 + i], kSoftThreads);
+    for (int i = 0; i < NS_LD; ++i) {
+      mbar_init(&bars[bLdFull + i], 1);
+      mbar_init(&bars[bLdEmpty + i], 4);
     }
-    mbar_init(&bars[kPFull], kSoftThreads);
-    mbar_init(&bars[kPVDone], 1);
-    mbar_init(&bars[kFinal], 1);
+    for (int i = 0; i < NS_KV; ++i) {
+      mbar_init(&bars[bKvFull + i], 4);
+      mbar_init(&bars[bKvEmpty + i], 1);
+    }
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(&bars[bQReady + x], 4);
+      mbar_init(&bars[bSFull + x], 1);
+      mbar_init(&bars[bPFull + x], 4);
+      mbar_init(&bars[bOFinal + x], 1);
+    }
+    mbar_init(&bars[bMmaDone], 1);
     *abort = 0;
     fence_mbar_init();
   }
@@ -211,71 +229,75 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
     tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
   }
+  if (warp == kProdWarp && lane == 0) {
+    prefetch_tmap(&a.tm_kc);
+    prefetch_tmap(&a.tm_vc);
+    if (a.sink_tokens > 0) {
+      prefetch_tmap(&a.tm_ks);
+      prefetch_tmap(&a.tm_vs);
+    }
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp < 4) {
-    // ------------------------------------------------------------ converters
-    const int r = tid;
+  if (warp < 8) {
+    // ------------------------------------------------------------ softmax (Q tile x)
+    const int x = warp >> 2;
+    const int r = tid - x * BM;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t tQ = tmem + lane_off + kColQ + 64 * x;
+    const uint32_t tO = tmem + lane_off + kColO + 128 * x;
+    const uint32_t tS = tmem + lane_off + kColS + 64 * x;
+    const int qi = q0 + x * BM + r;
     {
-      const int qi = q0 + r;
-      const uint32_t qb = sbase + kOffQ;
+      uint32_t qw[64];
       if (qi < a.Lq) {
         const uint16_t* src = a.q + b * a.q_batch_stride + static_cast<int64_t>(qi) * a.q_tok_stride +
                               static_cast<int64_t>(h) * D;
-        uint4 v[16];
 #pragma unroll
-        for (int c = 0; c < 16; ++c) v[c] = ld_global_nc_v4(src + 8 * c);
-#pragma unroll
-        for (int c = 0; c < 16; ++c) st_shared_v4(qb + tile_off(r, c), v[c]);
+        for (int c = 0; c < 16; ++c) {
+          uint4 v = ld_global_nc_v4(src + 8 * c);
+          qw[4 * c] = v.x;
+          qw[4 * c + 1] = v.y;
+          qw[4 * c + 2] = v.z;
+          qw[4 * c + 3] = v.w;
+        }
       } else {
 #pragma unroll
-        for (int c = 0; c < 16; ++c) st_shared_v4(qb + tile_off(r, c), make_uint4(0, 0, 0, 0));
+        for (int c = 0; c < 64; ++c) qw[c] = 0u;
       }
-      fence_proxy_async_smem();
-      mbar_arrive(&bars[kQFull]);
+      tmem_st32(tQ, reinterpret_cast<const uint32_t(&)[32]>(qw[0]));
+      tmem_st32(tQ + 32, reinterpret_cast<const uint32_t(&)[32]>(qw[32]));
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[bQReady + x]);
     }
-    for (int j = 0; j < nkv; ++j) {
-      const int buf = j & 1;
-      if (j >= 2 && !mbar_wait_warp(&bars[kKVEmpty0 + buf], ((j >> 1) - 1) & 1, abort, &g_attn_status)) break;
-      const int jt = j * BN + r;
-      convert_row<L>(a, a.kc, a.ks, a.ksink, b, h, jt, sbase + kOffK + buf * kTile, r);
-      convert_row<L>(a, a.vc, a.vs, a.vsink, b, h, jt, sbase + kOffV + buf * kTile, r);
-      fence_proxy_async_smem();
-      mbar_arrive(&bars[kKVFull0 + buf]);
-    }
-  } else if (warp < 8) {
-    // ------------------------------------------------------------ softmax
-    const int r = tid - kConvThreads;                 // Q row = TMEM lane
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
-    const uint32_t pb = sbase + kOffP;
     float m = -INFINITY, l = 0.0f;
     bool ok = true;
-    for (int j = 0; j < nkv && ok; ++j) {
-      const int buf = j & 1;
-      if (!mbar_wait_warp(&bars[kSFull0 + buf], (j >> 1) & 1, abort, &g_attn_status)) { ok = false; break; }
+    for (int j = 0; j < nkv; ++j) {
+      if (!mbar_wait_warp(&bars[bSFull + x], j & 1, abort, &g_attn_status)) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
-      const uint32_t sb = lane_base + kColS + buf * 128;
+      uint32_t s0[32], s1[32];
+      tmem_ld32x2_wait(tS, tS + 32, s0, s1);
       const int valid = min(BN, a.Lk - j * BN);
-      // pass 1: row max of S (64 columns per TMEM round trip)
       float mx = -INFINITY;
+      if (valid == BN) {
 #pragma unroll
-      for (int k = 0; k < 2; ++k) {
-        uint32_t s0[32], s1[32];
-        tmem_ld32(sb + 64 * k, s0);
-        tmem_ld32(sb + 64 * k + 32, s1);
-        tmem_wait_ld();
+        for (int c = 0; c < 32; ++c) mx = fmaxf(mx, fmaxf(__uint_as_float(s0[c]), __uint_as_float(s1[c])));
+      } else {
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
-          if (64 * k + c < valid) mx = fmaxf(mx, __uint_as_float(s0[c]));
-          if (64 * k + 32 + c < valid) mx = fmaxf(mx, __uint_as_float(s1[c]));
+          if (c < valid) mx = fmaxf(mx, __uint_as_float(s0[c]));
+          if (32 + c < valid) mx = fmaxf(mx, __uint_as_float(s1[c]));
         }
       }
       const float mt = mx * a.scale_log2;
-      // P_j goes to the single P buffer and O may be rescaled: PV_{j-1} must be done
-      if (j > 0 && !mbar_wait_warp(&bars[kPVDone], (j - 1) & 1, abort, &g_attn_status)) { ok = false; break; }
       bool rescale = false;
       float alpha = 1.0f;
       if (j == 0) {
@@ -287,61 +309,51 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
         l *= alpha;
       }
       if (__any_sync(0xffffffffu, rescale)) {
-        tc_fence_after();
+        // O_x is complete up to PV_x(j-1): S_x(j) was issued after it
 #pragma unroll 1
         for (int k = 0; k < 4; ++k) {
           uint32_t o[32];
-          tmem_ld32(lane_base + kColO + 32 * k, o);
-          tmem_wait_ld();
+          tmem_ld32_wait(tO + 32 * k, o);
 #pragma unroll
           for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
-          tmem_st32(lane_base + kColO + 32 * k, o);
+          tmem_st32(tO + 32 * k, o);
         }
-        tmem_wait_st();
       }
-      // pass 2: P = exp2(S * scale_log2 - m), bf16 into the swizzled P tile
       const float nm = -m;
       float sum = 0.0f;
+      uint32_t pw[32];
 #pragma unroll
-      for (int k = 0; k < 2; ++k) {
-        uint32_t s0[32], s1[32];
-        tmem_ld32(sb + 64 * k, s0);
-        tmem_ld32(sb + 64 * k + 32, s1);
-        tmem_wait_ld();
-#pragma unroll
-        for (int c8 = 0; c8 < 8; ++c8) {
-          float p[8];
-#pragma unroll
-          for (int t = 0; t < 8; ++t) {
-            const int cc = 8 * c8 + t;  // column within this 64-column half
-            const float sv = __uint_as_float(cc < 32 ? s0[cc] : s1[cc - 32]);
-            const float e = ex2(fmaf(sv, a.scale_log2, nm));
-            p[t] = (64 * k + cc < valid) ? e : 0.0f;
-            sum += p[t];
-          }
-          st_shared_v4(pb + tile_off(r, 8 * k + c8),
-                       make_uint4(pack_bf16x2(p[0], p[1]), pack_bf16x2(p[2], p[3]), pack_bf16x2(p[4], p[5]),
-                                  pack_bf16x2(p[6], p[7])));
+      for (int c = 0; c < 16; ++c) {
+        float p0 = ex2(fmaf(__uint_as_float(s0[2 * c]), a.scale_log2, nm));
+        float p1 = ex2(fmaf(__uint_as_float(s0[2 * c + 1]), a.scale_log2, nm));
+        float p2 = ex2(fmaf(__uint_as_float(s1[2 * c]), a.scale_log2, nm));
+        float p3 = ex2(fmaf(__uint_as_float(s1[2 * c + 1]), a.scale_log2, nm));
+        if (valid < BN) {
+          p0 = (2 * c < valid) ? p0 : 0.0f;
+          p1 = (2 * c + 1 < valid) ? p1 : 0.0f;
+          p2 = (32 + 2 * c < valid) ? p2 : 0.0f;
+          p3 = (33 + 2 * c < valid) ? p3 : 0.0f;
         }
+        sum += (p0 + p1) + (p2 + p3);
+        pw[c] = pack_bf16x2(p0, p1);
+        pw[16 + c] = pack_bf16x2(p2, p3);
       }
-      tc_fence_before();
-      mbar_arrive(&bars[kSEmpty0 + buf]);
       l += sum;
-      fence_proxy_async_smem();
+      tmem_st32(tS, pw);  // P_x(j), 64 bf16 = 32 columns, over S_x(j)
+      tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&bars[kPFull]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[bPFull + x]);
     }
-    if (ok && nkv > 0 && mbar_wait_warp(&bars[kPVDone], (nkv - 1) & 1, abort, &g_attn_status)) {
+    if (ok && mbar_wait_warp(&bars[bOFinal + x], 0, abort, &g_attn_status)) {
       tc_fence_after();
-      const int qi = q0 + r;
       const float inv = 1.0f / l;
       uint16_t* dst = a.out + b * a.o_batch_stride + static_cast<int64_t>(qi) * a.o_tok_stride +
                       static_cast<int64_t>(h) * D;
 #pragma unroll 1
       for (int k = 0; k < 4; ++k) {
         uint32_t o[32];
-        tmem_ld32(lane_base + kColO + 32 * k, o);
-        tmem_wait_ld();
+        tmem_ld32_wait(tO + 32 * k, o);
         if (qi < a.Lq) {
 #pragma unroll
           for (int c = 0; c < 4; ++c)
@@ -353,48 +365,134 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
         }
       }
     }
-  } else {
+  } else if (warp < kProdWarp) {
+    // ------------------------------------------------------------ converters
+    const int t = tid - kConvWarp0 * 32;
+    const int r = t & (BN - 1);
+    const int is_v = t >> 6;
+    const uint16_t* scales = is_v ? a.vs : a.ks;
+    const uint32_t codes_base = sbase + (is_v ? kOffVC : kOffKC);
+    const uint32_t kv_base = sbase + (is_v ? kOffV : kOffK);
+    for (int j = 0; j < nkv; ++j) {
+      const int ls = j % NS_LD, ks = j % NS_KV;
+      const int jt = j * BN + r;
+      const int64_t tok = a.lo + jt;
+      const bool live = jt < a.Lk;
+      const bool coded = live && tok >= a.sink_tokens;
+      ScaleWords<L> sw;
+      if (coded) load_scale_words<L>(scales + ((static_cast<int64_t>(b) * a.cache_tokens + tok) * a.H + h) * L::G, sw);
+      if (!mbar_wait_warp(&bars[bLdFull + ls], (j / NS_LD) & 1, abort, &g_attn_status)) break;
+      if (j >= NS_KV && !mbar_wait_warp(&bars[bKvEmpty + ks], ((j / NS_KV) - 1) & 1, abort, &g_attn_status)) break;
+      const uint32_t dst = kv_base + ks * kKVTile;
+      if (!live) {
+#pragma unroll
+        for (int c = 0; c < 16; ++c) st_shared_v4(dst + tile_off(r, c), make_uint4(0, 0, 0, 0));
+      } else if (coded) {
+        const uint32_t src = codes_base + ls * kCodeTile + r * 64;
+        uint32_t w[16];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint4 v = ld_shared_v4(src + ((c ^ ((r >> 1) & 3)) << 4));
+          w[4 * c] = v.x;
+          w[4 * c + 1] = v.y;
+          w[4 * c + 2] = v.z;
+          w[4 * c + 3] = v.w;
+        }
+        uint32_t sp[L::G];
+        scale_pairs<L>(sw, sp);
+        deq_row<L>(w, sp, dst, r, std::make_integer_sequence<int, 16>{});
+      }
+      // sink rows were written into the tile by the TMA
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&bars[bLdEmpty + ls]);
+        mbar_arrive(&bars[bKvFull + ks]);
+      }
+    }
+  } else if (warp == kProdWarp) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      for (int j = 0; j < nkv; ++j) {
+        const int ls = j % NS_LD, ks = j % NS_KV;
+        if (j >= NS_LD && !mbar_wait(&bars[bLdEmpty + ls], ((j / NS_LD) - 1) & 1, abort, &g_attn_status)) break;
+        const int64_t t0 = a.lo + static_cast<int64_t>(j) * BN;
+        const int64_t t1 = a.lo + min(static_cast<int64_t>(j + 1) * BN, static_cast<int64_t>(a.Lk));
+        const bool has_sink = t0 < a.sink_tokens;
+        const bool has_codes = t1 > a.sink_tokens;
+        if (has_sink && j >= NS_KV &&
+            !mbar_wait(&bars[bKvEmpty + ks], ((j / NS_KV) - 1) & 1, abort, &g_attn_status))
+          break;
+        const uint32_t bytes = (has_codes ? 2u * kCodeTile : 0u) + (has_sink ? 2u * kKVTile : 0u);
+        mbar_arrive_expect_tx(&bars[bLdFull + ls], bytes);
+        if (has_codes) {
+          const int row = static_cast<int>(static_cast<int64_t>(b) * a.cache_tokens + t0);
+          tma_load_2d(sbase + kOffKC + ls * kCodeTile, &a.tm_kc, h * 64, row, &bars[bLdFull + ls]);
+          tma_load_2d(sbase + kOffVC + ls * kCodeTile, &a.tm_vc, h * 64, row, &bars[bLdFull + ls]);
+        }
+        if (has_sink) {
+          const int row = static_cast<int>(static_cast<int64_t>(b) * a.sink_tokens + t0);
+          const uint32_t kd = sbase + kOffK + ks * kKVTile, vd = sbase + kOffV + ks * kKVTile;
+          tma_load_2d(kd, &a.tm_ks, h * D, row, &bars[bLdFull + ls]);
+          tma_load_2d(kd + kAtom, &a.tm_ks, h * D + 64, row, &bars[bLdFull + ls]);
+          tma_load_2d(vd, &a.tm_vs, h * D, row, &bars[bLdFull + ls]);
+          tma_load_2d(vd + kAtom, &a.tm_vs, h * D + 64, row, &bars[bLdFull + ls]);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idS = idesc_bf16(BM, BN, 0);
       constexpr uint32_t idPV = idesc_bf16(BM, D, 1);
-      const uint32_t qaddr = sbase + kOffQ, paddr = sbase + kOffP;
-      bool ok = mbar_wait(&bars[kQFull], 0, abort, &g_attn_status);
-      auto issue_s = [&](int j) -> bool {
-        const int buf = j & 1;
-        if (!mbar_wait(&bars[kKVFull0 + buf], (j >> 1) & 1, abort, &g_attn_status)) return false;
-        if (j >= 2 && !mbar_wait(&bars[kSEmpty0 + buf], ((j >> 1) - 1) & 1, abort, &g_attn_status)) return false;
-        tc_fence_after();
-        const uint32_t kaddr = sbase + kOffK + buf * kTile;
+      auto issue_s = [&](int x, int j) {
+        const uint32_t kaddr = sbase + kOffK + (j % NS_KV) * kKVTile;
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t off = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
-          mma_bf16_ss(tmem + kColS + buf * 128, smem_desc_sw128(qaddr + off, 16, 1024),
-                      smem_desc_sw128(kaddr + off, 16, 1024), idS, kk > 0);
-        }
-        mma_commit(&bars[kSFull0 + buf]);
-        return true;
+        for (int kk = 0; kk < 8; ++kk)
+          mma_bf16_ts(tmem + kColS + 64 * x, tmem + kColQ + 64 * x + 8 * kk,
+                      smem_desc_sw128(kaddr + (kk >> 2) * kAtom + (kk & 3) * 32, 16, 1024), idS, kk > 0);
+        mma_commit(&bars[bSFull + x]);
       };
-      if (ok && nkv > 0) ok = issue_s(0);
-      for (int j = 0; j < nkv && ok; ++j) {
-        if (j + 1 < nkv && !(ok = issue_s(j + 1))) break;
-        if (!(ok = mbar_wait(&bars[kPFull], j & 1, abort, &g_attn_status))) break;
-        tc_fence_after();
-        const uint32_t vaddr = sbase + kOffV + (j & 1) * kTile;
+      auto issue_pv = [&](int x, int j) {
+        const uint32_t vaddr = sbase + kOffV + (j % NS_KV) * kKVTile;
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          // A = P (K-major over tokens), B = V (MN-major: rows are tokens, d contiguous)
-          const uint32_t aoff = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
-          const uint32_t boff = kk * 2048;  // 16 tokens = two 8-row groups
-          mma_bf16_ss(tmem + kColO, smem_desc_sw128(paddr + aoff, 16, 1024),
-                      smem_desc_sw128(vaddr + boff, BN * 128, 1024), idPV, (j > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < BN / 16; ++kk)
+          mma_bf16_ts(tmem + kColO + 128 * x, tmem + kColS + 64 * x + 8 * kk,
+                      smem_desc_sw128(vaddr + kk * 2048, kAtom, 1024), idPV, (j > 0 || kk > 0) ? 1u : 0u);
+      };
+      bool ok = mbar_wait(&bars[bQReady + 0], 0, abort, &g_attn_status) &&
+                mbar_wait(&bars[bQReady + 1], 0, abort, &g_attn_status) &&
+                mbar_wait(&bars[bKvFull + 0], 0, abort, &g_attn_status);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0);
+        issue_s(1, 0);
+      }
+      for (int j = 0; j < nkv && ok; ++j) {
+        if (!(ok = mbar_wait(&bars[bPFull + 0], j & 1, abort, &g_attn_status))) break;
+        tc_fence_after();
+        issue_pv(0, j);
+        const bool more = j + 1 < nkv;
+        if (more) {
+          if (!(ok = mbar_wait(&bars[bKvFull + (j + 1) % NS_KV], ((j + 1) / NS_KV) & 1, abort, &g_attn_status)))
+            break;
+          tc_fence_after();
+          issue_s(0, j + 1);
         }
-        mma_commit(&bars[kPVDone]);
-        mma_commit(&bars[kKVEmpty0 + (j & 1)]);
+        if (!(ok = mbar_wait(&bars[bPFull + 1], j & 1, abort, &g_attn_status))) break;
+        tc_fence_after();
+        issue_pv(1, j);
+        mma_commit(&bars[bKvEmpty + j % NS_KV]);
+        if (more) issue_s(1, j + 1);
+      }
+      if (ok) {
+        mma_commit(&bars[bOFinal + 0]);
+        mma_commit(&bars[bOFinal + 1]);
       }
       // all MMAs issued by this thread have completed before TMEM is released
-      mma_commit(&bars[kFinal]);
-      mbar_wait(&bars[kFinal], 0, abort, &g_attn_status);
+      mma_commit(&bars[bMmaDone]);
+      mbar_wait(&bars[bMmaDone], 0, abort, &g_attn_status);
     }
     __syncwarp();
   }
@@ -407,8 +505,42 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
   }
 }
 
+// ---------------------------------------------------------------- host side
+using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeFn encode_fn() {
+  static EncodeFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeFn>(p);
+  }
+  return fn;
+}
+
+// 2-D map over `rows` rows of `row_elems` elements (row stride `row_bytes`), box
+// box_x x box_y, given swizzle; out-of-range boxes are zero-filled.
+static int make_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, uint64_t row_elems,
+                    uint64_t row_bytes, uint64_t rows, uint32_t box_x, uint32_t box_y, CUtensorMapSwizzle sw,
+                    const char* what) {
+  EncodeFn fn = encode_fn();
+  KVQ_REQUIRE(fn != nullptr, KVQ_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t dims[2] = {row_elems, rows};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_x, box_y};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  KVQ_REQUIRE(r == CUDA_SUCCESS, KVQ_ERR_CUDA, "cuTensorMapEncodeTiled(%s) failed with %d", what, (int)r);
+  return KVQ_OK;
+}
+
 template <class L>
-int launch(const Args& a, int n_qtiles, int batch, cudaStream_t st) {
+int launch(const Args& a, int n_ctas, int batch, cudaStream_t st) {
   static bool configured[64];
   int dev = 0;
   cudaGetDevice(&dev);
@@ -421,7 +553,7 @@ int launch(const Args& a, int n_qtiles, int batch, cudaStream_t st) {
     }
     configured[dev] = true;
   }
-  dim3 grid(n_qtiles, a.H, batch);
+  dim3 grid(n_ctas, a.H, batch);
   attention_kernel<L><<<grid, kThreads, kSmemBytes, st>>>(a);
   return check_launch("kvq_attention");
 }
@@ -446,7 +578,9 @@ extern "C" int kvq_attention(const void* q, int64_t q_token_stride, const void* 
   KVQ_REQUIRE(0 <= lo && lo < hi && hi <= cache_tokens, KVQ_ERR_ARG,
               "window [%lld, %lld) is empty or outside the cache of %lld tokens", (long long)lo, (long long)hi,
               (long long)cache_tokens);
-  KVQ_REQUIRE(hi - lo <= (int64_t)1 << 30 && n_q <= (int64_t)1 << 30, KVQ_ERR_ARG, "sequence too long");
+  KVQ_REQUIRE(n_q <= (int64_t)1 << 30, KVQ_ERR_ARG, "too many queries");
+  KVQ_REQUIRE((int64_t)batch * cache_tokens < ((int64_t)1 << 31) - 256, KVQ_ERR_ARG,
+              "batch * cache_tokens must stay below 2^31");
   KVQ_REQUIRE(sink_tokens >= 0 && sink_tokens <= cache_tokens, KVQ_ERR_ARG, "bad sink_tokens");
   KVQ_REQUIRE(sink_tokens == 0 || (k_sink && v_sink), KVQ_ERR_ARG, "sink_tokens > 0 needs both sink buffers");
   GroupMap map;
@@ -468,37 +602,49 @@ extern "C" int kvq_attention(const void* q, int64_t q_token_stride, const void* 
               KVQ_ERR_ALIGN, "scales must be %d-byte aligned for %d groups", sa, n_groups);
   int rc = require_sm100();
   if (rc) return rc;
+
   attn::Args a;
+  memset(&a, 0, sizeof(a));
+  const uint64_t rows = static_cast<uint64_t>(batch) * cache_tokens;
+  rc = attn::make_map(&a.tm_kc, k_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)n_heads * 64,
+                      (uint64_t)n_heads * 64, rows, 64, attn::BN, CU_TENSOR_MAP_SWIZZLE_64B, "k codes");
+  if (rc) return rc;
+  rc = attn::make_map(&a.tm_vc, v_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)n_heads * 64,
+                      (uint64_t)n_heads * 64, rows, 64, attn::BN, CU_TENSOR_MAP_SWIZZLE_64B, "v codes");
+  if (rc) return rc;
+  if (sink_tokens > 0) {
+    const uint64_t srows = static_cast<uint64_t>(batch) * sink_tokens;
+    rc = attn::make_map(&a.tm_ks, k_sink, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)n_heads * 128,
+                        (uint64_t)n_heads * 256, srows, 64, attn::BN, CU_TENSOR_MAP_SWIZZLE_128B, "k sink");
+    if (rc) return rc;
+    rc = attn::make_map(&a.tm_vs, v_sink, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)n_heads * 128,
+                        (uint64_t)n_heads * 256, srows, 64, attn::BN, CU_TENSOR_MAP_SWIZZLE_128B, "v sink");
+    if (rc) return rc;
+  }
   a.q = static_cast<const uint16_t*>(q);
   a.q_tok_stride = q_token_stride;
   a.q_batch_stride = q_token_stride * n_q;
-  a.kc = static_cast<const uint8_t*>(k_codes);
   a.ks = static_cast<const uint16_t*>(k_scales);
-  a.ksink = static_cast<const uint16_t*>(k_sink);
-  a.vc = static_cast<const uint8_t*>(v_codes);
   a.vs = static_cast<const uint16_t*>(v_scales);
-  a.vsink = static_cast<const uint16_t*>(v_sink);
   a.cache_tokens = cache_tokens;
   a.sink_tokens = sink_tokens;
   a.lo = lo;
   a.Lk = static_cast<int>(hi - lo);
   a.Lq = static_cast<int>(n_q);
   a.H = n_heads;
-  a.G = n_groups;
   a.out = static_cast<uint16_t*>(out);
   a.o_tok_stride = out_token_stride;
   a.o_batch_stride = out_token_stride * n_q;
   const float sc = softmax_scale > 0.0f ? softmax_scale : 1.0f / sqrtf(static_cast<float>(head_dim));
   a.scale_log2 = sc * 1.4426950408889634f;
-  a.map = map;
-  const int tiles = static_cast<int>((n_q + attn::BM - 1) / attn::BM);
+  const int ctas = static_cast<int>((n_q + 2 * attn::BM - 1) / (2 * attn::BM));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   switch (layout) {
-    case kLayoutBands: return attn::launch<LayoutBands>(a, tiles, batch, st);
-    case kLayoutBands2: return attn::launch<LayoutBands2>(a, tiles, batch, st);
-    case kLayoutBands4: return attn::launch<LayoutBands4>(a, tiles, batch, st);
-    case kLayoutBlind32: return attn::launch<LayoutBlind32>(a, tiles, batch, st);
-    case kLayoutBlind64: return attn::launch<LayoutBlind64>(a, tiles, batch, st);
+    case kLayoutBands: return attn::launch<LayoutBands>(a, ctas, batch, st);
+    case kLayoutBands2: return attn::launch<LayoutBands2>(a, ctas, batch, st);
+    case kLayoutBands4: return attn::launch<LayoutBands4>(a, ctas, batch, st);
+    case kLayoutBlind32: return attn::launch<LayoutBlind32>(a, ctas, batch, st);
+    case kLayoutBlind64: return attn::launch<LayoutBlind64>(a, ctas, batch, st);
     default: break;
   }
   set_error("internal: unhandled layout %d", layout);
