@@ -4,18 +4,20 @@
 // torch path, bit-exact. The reference's Triton kernels (quant_kv_kernels.py:33-84)
 // round ties away from zero and are NOT the parity target.
 //
-// Quantize, specialised layouts (head_dim 128), one CTA of 128 threads per tile of
-// 128 (token, head) rows:
-//   1. the 32 KB input tile is loaded with coalesced 16-byte loads into shared
-//      memory, chunk c of row r stored at slot c ^ (r & 7), so that the per-row
-//      reads of step 2 are bank-conflict free;
+// Quantize, specialised layouts (head_dim 128): persistent CTAs of 128 threads
+// (three per SM for int4 codes, two for int8) walk 128-row tiles of (token, head) rows with a grid stride:
+//   1. each thread keeps the next tile's input in flight (cp.async, 16 bytes per
+//      copy, 2 stages), chunk c of row r stored at slot c ^ (r & 7) so that the
+//      per-row reads of step 2 are bank-conflict free;
 //   2. thread r owns row r: 64 bf16x2 words in registers, per-group absmax on
-//      packed bf16x2 (NaN-propagating), one IEEE divide and one correctly
-//      rounded reciprocal per group, then per element the division-free code
+//      packed bf16x2 (NaN-propagating), the group scale amax / qmax by two FMAs
+//      (equal to the IEEE divide for every bf16 amax, kvqo_check_scale_div), one
+//      reciprocal per group (approximation + Newton step, within one ulp), then
+//      per element the
+//      division-free code
 //        y0 = x*r, rem = fma(-y0, s, x), y = fma(rem, r, y0), code = rne(y)
 //      which equals rne(x / s) for every finite bf16 pair (x, amax) with
-//      amax >= 2^-100 (exhaustively checked by the oracle's
-//      kvqo_check_fast_codes); other groups use the exact divide;
+//      amax >= 2^-100 (kvqo_check_fast_codes); other groups use the exact divide;
 //      rne and the +8 / +128 offset come from one add of a magic constant;
 //   3. codes and scales are staged in shared memory and written out with
 //      coalesced stores; rows inside the sink are copied to the bf16 sink buffer
@@ -84,6 +86,23 @@ struct QuantConsts {
   static constexpr int kCodeBytes = BITS == 4 ? kQD / 2 : kQD;  // per row
 };
 
+// Group scale s = amax / qmax without a divide: q0 = amax * r, rem = amax - q0 * qmax
+// (FMA), s = q0 + rem * r (FMA), r = RN(1/qmax). Equal to the IEEE quotient for
+// every positive finite bf16 amax (exhaustively checked by the oracle's
+// kvqo_check_scale_div); non-finite amax take the IEEE divide.
+template <int QMAX>
+__device__ __forceinline__ float group_scale(float amax) {
+  if (!(amax <= 3.0e38f)) return __fdiv_rn(amax, static_cast<float>(QMAX));
+  const float r = QMAX == 7 ? 0.142857149243354797f : 0.00787401571869850159f;
+  const float q0 = __fmul_rn(amax, r);
+  const float rem = __fmaf_rn(-q0, static_cast<float>(QMAX), amax);
+  return __fmaf_rn(rem, r, q0);
+}
+
+// __byte_perm selectors that replace byte p of the first operand with byte 0 of
+// the second and keep the other three
+__device__ constexpr uint32_t kInsertByte[4] = {0x3214u, 0x3240u, 0x3410u, 0x4210u};
+
 template <int LO, int HI, int BITS>
 __device__ __forceinline__ void quant_group(const uint32_t (&w)[64], uint32_t (&ow)[BITS == 4 ? 16 : 32],
                                             uint16_t& scale_out) {
@@ -98,22 +117,33 @@ __device__ __forceinline__ void quant_group(const uint32_t (&w)[64], uint32_t (&
     float a = __uint_as_float(lo), b = __uint_as_float(hi);
     amax = (a != a || b != b) ? __uint_as_float(0x7FC00000u) : fmaxf(a, b);
   }
-  float s = __fdiv_rn(amax, static_cast<float>(C::kQmax));
+  float s = group_scale<C::kQmax>(amax);
   s = (s > 0.0f) ? s : 1.0f;  // quant_kv.py:152 (also maps NaN to 1, like torch.where)
   scale_out = f32_to_bf16_bits(s);
   const bool fast = (amax >= 0x1p-100f) && (amax <= 3.0e38f);
   if (fast) {
-    const float r = __frcp_rn(s);
+    // reciprocal within one ulp of 1/s: hardware approximation + one Newton step
+    // (the code formula holds for any such r, kvqo_check_fast_codes_rcp)
+    float r;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(s));
+    r = __fmaf_rn(r, __fmaf_rn(-s, r, 1.0f), r);
+    // the per-element chain on packed f32x2: two channels per instruction
+    const float2 r2 = make_float2(r, r), ns2 = make_float2(-s, -s);
+    const float2 mg2 = make_float2(C::kMagic, C::kMagic);
 #pragma unroll
     for (int k = LO / 2; k < HI / 2; ++k) {
-      uint32_t c0 = code_fast(bf16lo_to_f32(w[k]), s, r, C::kMagic);
-      uint32_t c1 = code_fast(bf16hi_to_f32(w[k]), s, r, C::kMagic);
+      const float2 x = make_float2(bf16lo_to_f32(w[k]), bf16hi_to_f32(w[k]));
+      const float2 y0 = __fmul2_rn(x, r2);
+      const float2 rem = __ffma2_rn(y0, ns2, x);
+      const float2 t = __fadd2_rn(__ffma2_rn(rem, r2, y0), mg2);
+      const uint32_t c0 = __float_as_uint(t.x), c1 = __float_as_uint(t.y);
       if constexpr (BITS == 4) {
-        uint32_t byte = (c0 & 0xFu) | ((c1 & 0xFu) << 4);
-        ow[k >> 2] |= byte << (8 * (k & 3));
+        // low byte of c0 + 16 * c1 is the packed pair (code bytes are < 16)
+        const uint32_t pair = c0 + (c1 << 4);
+        ow[k >> 2] = __byte_perm(ow[k >> 2], pair, kInsertByte[k & 3]);
       } else {
-        uint32_t half = (c0 & 0xFFu) | ((c1 & 0xFFu) << 8);
-        ow[k >> 1] |= half << (16 * (k & 1));
+        const uint32_t half = __byte_perm(c0, c1, 0x0040);
+        ow[k >> 1] = __byte_perm(ow[k >> 1], half, (k & 1) ? 0x5410u : 0x3254u);
       }
     }
   } else {
@@ -139,89 +169,132 @@ __device__ __forceinline__ void quant_row(const uint32_t (&w)[64], uint32_t (&ow
   (quant_group<L::E[Gs], L::E[Gs + 1], BITS>(w, ow, sc[Gs]), ...);
 }
 
+__device__ __forceinline__ void cp_async16(uint32_t dst_smem, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst_smem), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+template <int BITS>
+struct PipeCfg {
+  static constexpr int kStages = 2;  // keeps three CTAs per SM
+};
+
 template <class L, int BITS>
-__global__ void __launch_bounds__(kQT) quantize_rows_fast(QuantArgs a) {
+constexpr int pipe_smem_bytes() {
+  return PipeCfg<BITS>::kStages * kQT * 256 + kQT * QuantConsts<BITS>::kCodeBytes + ((kQT * L::G * 2 + 15) / 16) * 16;
+}
+
+// Persistent CTAs walk the 128-row tiles with a grid stride; each thread keeps
+// the next kStages-1 tiles' input in flight (cp.async, 16 bytes per copy, into
+// the XOR-swizzled layout) while it quantizes its row of the current tile.
+template <class L, int BITS>
+__global__ void __launch_bounds__(kQT, 3) quantize_rows_pipe(QuantArgs a, int64_t n_tiles) {
   using C = QuantConsts<BITS>;
   constexpr int G = L::G;
-  constexpr int CW = C::kCodeBytes;           // code bytes per row
-  constexpr int CCH = CW / 16;                // 16-byte code chunks per row
+  constexpr int S = PipeCfg<BITS>::kStages;
+  constexpr int CW = C::kCodeBytes;
+  constexpr int CCH = CW / 16;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint4* sm_in = reinterpret_cast<uint4*>(smem_raw);                       // kQT * 16 chunks
-  uint4* sm_codes = reinterpret_cast<uint4*>(smem_raw + kQT * 256);        // kQT * CCH chunks
-  uint16_t* sm_sc = reinterpret_cast<uint16_t*>(smem_raw + kQT * 256 + kQT * CW);  // kQT * G
-
-  const int64_t row0 = static_cast<int64_t>(blockIdx.x) * kQT;
-  const int nrows = static_cast<int>(min(static_cast<int64_t>(kQT), a.n_rows - row0));
+  uint4* sm_in = reinterpret_cast<uint4*>(smem_raw);                                   // S x kQT x 16 chunks
+  uint4* sm_codes = reinterpret_cast<uint4*>(smem_raw + S * kQT * 256);                // kQT x CCH
+  uint16_t* sm_sc = reinterpret_cast<uint16_t*>(smem_raw + S * kQT * 256 + kQT * CW);  // kQT x G
   const int tid = threadIdx.x;
+  const uint32_t in_base = static_cast<uint32_t>(__cvta_generic_to_shared(sm_in));
 
-  // 1. coalesced tile load
-#pragma unroll 8
-  for (int i = tid; i < nrows * 16; i += kQT) {
-    const int r = i >> 4, c = i & 15;
-    const uint16_t* src = x_row_ptr(a, row0 + r, kQD) + c * 8;
-    sm_in[r * 16 + (c ^ (r & 7))] = ld_global_nc_v4(src);
-  }
-  __syncthreads();
-
-  // 2. one row per thread
-  if (tid < nrows) {
-    uint32_t w[64];
-#pragma unroll
-    for (int c = 0; c < 16; ++c) {
-      uint4 v = sm_in[tid * 16 + (c ^ (tid & 7))];
-      w[4 * c + 0] = v.x;
-      w[4 * c + 1] = v.y;
-      w[4 * c + 2] = v.z;
-      w[4 * c + 3] = v.w;
-    }
-    uint32_t ow[BITS == 4 ? 16 : 32];
-#pragma unroll
-    for (int k = 0; k < (BITS == 4 ? 16 : 32); ++k) ow[k] = 0;
-    uint16_t sc[G];
-    quant_row<L, BITS>(w, ow, sc, std::make_integer_sequence<int, G>{});
-    // stage codes: chunk c of row r at slot c ^ swz(r) (conflict-free both ways)
-#pragma unroll
-    for (int c = 0; c < CCH; ++c) {
-      const int slot = (BITS == 4) ? (c ^ ((tid >> 1) & 3)) : (c ^ (tid & 7));
-      sm_codes[tid * CCH + slot] = make_uint4(ow[4 * c], ow[4 * c + 1], ow[4 * c + 2], ow[4 * c + 3]);
-    }
-#pragma unroll
-    for (int g = 0; g < G; ++g) sm_sc[tid * G + g] = sc[g];
-  }
-  __syncthreads();
-
-  // 3a. codes: nrows * CW contiguous bytes
-  {
-    uint4* dst = reinterpret_cast<uint4*>(a.codes + row0 * CW);
-    for (int i = tid; i < nrows * CCH; i += kQT) {
-      const int r = i / CCH, c = i % CCH;
-      const int slot = (BITS == 4) ? (c ^ ((r >> 1) & 3)) : (c ^ (r & 7));
-      st_global_v4(dst + i, sm_codes[r * CCH + slot]);
-    }
-  }
-  // 3b. scales: nrows * G contiguous bf16, any 2-byte alignment
-  {
-    uint16_t* dst = a.scales + row0 * G;
-    const int n = nrows * G;
-    if ((reinterpret_cast<uintptr_t>(dst) & 15) == 0 && (n % 8) == 0) {
-      const uint4* s4 = reinterpret_cast<const uint4*>(sm_sc);
-      for (int i = tid; i < n / 8; i += kQT) st_global_v4(reinterpret_cast<uint4*>(dst) + i, s4[i]);
-    } else if ((reinterpret_cast<uintptr_t>(dst) & 3) == 0 && (n % 2) == 0) {
-      const uint32_t* s2 = reinterpret_cast<const uint32_t*>(sm_sc);
-      for (int i = tid; i < n / 2; i += kQT) reinterpret_cast<uint32_t*>(dst)[i] = s2[i];
-    } else {
-      for (int i = tid; i < n; i += kQT) dst[i] = sm_sc[i];
-    }
-  }
-  // 3c. sink rows: exact bf16 copy (quant_kv.py:213-215)
-  if (a.sink != nullptr && row0 < a.sink_rows) {
-    const int ns = static_cast<int>(min(static_cast<int64_t>(nrows), a.sink_rows - row0));
-    uint4* dst = reinterpret_cast<uint4*>(a.sink + row0 * kQD);
-    for (int i = tid; i < ns * 16; i += kQT) {
+  auto issue = [&](int64_t tile, int stage) {
+    const int64_t row0 = tile * kQT;
+    const int nrows = static_cast<int>(min(static_cast<int64_t>(kQT), a.n_rows - row0));
+#pragma unroll 4
+    for (int i = tid; i < kQT * 16; i += kQT) {
       const int r = i >> 4, c = i & 15;
-      st_global_v4(dst + i, sm_in[r * 16 + (c ^ (r & 7))]);
+      if (r < nrows) {
+        const uint16_t* src = x_row_ptr(a, row0 + r, kQD) + c * 8;
+        cp_async16(in_base + (((stage * kQT + r) * 16 + (c ^ (r & 7))) << 4), src);
+      }
     }
+  };
+
+  const int64_t first = blockIdx.x;
+#pragma unroll
+  for (int s = 0; s < S - 1; ++s) {
+    const int64_t t = first + static_cast<int64_t>(s) * gridDim.x;
+    if (t < n_tiles) issue(t, s);
+    cp_async_commit();
   }
+  for (int64_t k = 0;; ++k) {
+    const int64_t tile = first + k * gridDim.x;
+    if (tile >= n_tiles) break;
+    {
+      const int64_t tn = tile + static_cast<int64_t>(S - 1) * gridDim.x;
+      if (tn < n_tiles) issue(tn, static_cast<int>((k + S - 1) % S));
+      cp_async_commit();
+    }
+    cp_async_wait<S - 1>();
+    __syncthreads();
+    const int stage = static_cast<int>(k % S);
+    const uint4* tin = sm_in + stage * kQT * 16;
+    const int64_t row0 = tile * kQT;
+    const int nrows = static_cast<int>(min(static_cast<int64_t>(kQT), a.n_rows - row0));
+    if (tid < nrows) {
+      uint32_t w[64];
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        uint4 v = tin[tid * 16 + (c ^ (tid & 7))];
+        w[4 * c + 0] = v.x;
+        w[4 * c + 1] = v.y;
+        w[4 * c + 2] = v.z;
+        w[4 * c + 3] = v.w;
+      }
+      uint32_t ow[BITS == 4 ? 16 : 32];
+#pragma unroll
+      for (int q = 0; q < (BITS == 4 ? 16 : 32); ++q) ow[q] = 0;
+      uint16_t sc[G];
+      quant_row<L, BITS>(w, ow, sc, std::make_integer_sequence<int, G>{});
+#pragma unroll
+      for (int c = 0; c < CCH; ++c) {
+        const int slot = (BITS == 4) ? (c ^ ((tid >> 1) & 3)) : (c ^ (tid & 7));
+        sm_codes[tid * CCH + slot] = make_uint4(ow[4 * c], ow[4 * c + 1], ow[4 * c + 2], ow[4 * c + 3]);
+      }
+#pragma unroll
+      for (int g = 0; g < G; ++g) sm_sc[tid * G + g] = sc[g];
+    }
+    __syncthreads();
+    {
+      uint4* dst = reinterpret_cast<uint4*>(a.codes + row0 * CW);
+      for (int i = tid; i < nrows * CCH; i += kQT) {
+        const int r = i / CCH, c = i % CCH;
+        const int slot = (BITS == 4) ? (c ^ ((r >> 1) & 3)) : (c ^ (r & 7));
+        st_global_v4(dst + i, sm_codes[r * CCH + slot]);
+      }
+    }
+    {
+      uint16_t* dst = a.scales + row0 * G;
+      const int n = nrows * G;
+      if ((reinterpret_cast<uintptr_t>(dst) & 15) == 0 && (n % 8) == 0) {
+        const uint4* s4 = reinterpret_cast<const uint4*>(sm_sc);
+        for (int i = tid; i < n / 8; i += kQT) st_global_v4(reinterpret_cast<uint4*>(dst) + i, s4[i]);
+      } else if ((reinterpret_cast<uintptr_t>(dst) & 3) == 0 && (n % 2) == 0) {
+        const uint32_t* s2 = reinterpret_cast<const uint32_t*>(sm_sc);
+        for (int i = tid; i < n / 2; i += kQT) reinterpret_cast<uint32_t*>(dst)[i] = s2[i];
+      } else {
+        for (int i = tid; i < n; i += kQT) dst[i] = sm_sc[i];
+      }
+    }
+    if (a.sink != nullptr && row0 < a.sink_rows) {
+      const int ns = static_cast<int>(min(static_cast<int64_t>(nrows), a.sink_rows - row0));
+      uint4* dst = reinterpret_cast<uint4*>(a.sink + row0 * kQD);
+      for (int i = tid; i < ns * 16; i += kQT) {
+        const int r = i >> 4, c = i & 15;
+        st_global_v4(dst + i, tin[r * 16 + (c ^ (r & 7))]);
+      }
+    }
+    __syncthreads();  // the stage and the staging buffers are reused by later tiles
+  }
+  cp_async_wait<0>();
 }
 
 // ---------------------------------------------------------------- generic quantize
@@ -335,6 +408,148 @@ __global__ void __launch_bounds__(256) dequantize_rows(DequantArgs a, GroupMap m
   }
 }
 
+// Dequantize, specialised layouts (head_dim 128, int4): persistent CTAs of 128
+// threads walk 128-row tiles. The next tiles' codes are in flight (cp.async into a
+// 64B-swizzled stage) while each thread turns its row into 128 bf16: pair (2i,
+// 2i+1) = byte i becomes bf16x2 (128 + lo, 128 + hi) by a byte permute and a
+// mask/or, minus 136 (exact), times the group's (s, s) -- the exact product
+// rounded to bf16, i.e. bf16(float(q) * float(scale)) (quant_kv.py:174-175). Rows
+// inside the sink are copied from the bf16 sink. The tile is staged XOR-swizzled
+// in shared memory and written out with coalesced 16-byte stores.
+constexpr int kDStages = 3;
+
+__device__ __forceinline__ uint32_t bf16x2_sub(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t bf16x2_mul(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+template <class L>
+__host__ __device__ constexpr int chan_group(int ch) {
+  int g = 0;
+  while (g + 1 < L::G && ch >= L::E[g + 1]) ++g;
+  return g;
+}
+
+template <class L, int C>
+__device__ __forceinline__ uint4 deq_word(uint32_t w, const uint32_t (&sp)[L::G]) {
+  const uint32_t ws = w >> 4;
+  uint32_t o[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) o[i] = (__byte_perm(w, ws, static_cast<uint32_t>(((4 + i) << 8) | i)) & 0x000F000Fu) | 0x43004300u;
+  constexpr uint32_t k136 = 0x43084308u;  // bf16x2 (136, 136)
+  return make_uint4(bf16x2_mul(bf16x2_sub(o[0], k136), sp[chan_group<L>(8 * C + 0)]),
+                    bf16x2_mul(bf16x2_sub(o[1], k136), sp[chan_group<L>(8 * C + 2)]),
+                    bf16x2_mul(bf16x2_sub(o[2], k136), sp[chan_group<L>(8 * C + 4)]),
+                    bf16x2_mul(bf16x2_sub(o[3], k136), sp[chan_group<L>(8 * C + 6)]));
+}
+
+template <class L, int... Cs>
+__device__ __forceinline__ void deq_row_to(uint4* out_row, int r, const uint32_t (&w)[16], const uint32_t (&sp)[L::G],
+                                           std::integer_sequence<int, Cs...>) {
+  ((out_row[Cs ^ (r & 7)] = deq_word<L, Cs>(w[Cs], sp)), ...);
+}
+
+template <class L>
+__global__ void __launch_bounds__(kQT, 3) dequantize_rows_pipe(DequantArgs a, int64_t n_tiles) {
+  constexpr int G = L::G;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint4* sm_out = reinterpret_cast<uint4*>(smem_raw);                  // kQT x 16 chunks
+  const uint32_t code_base = static_cast<uint32_t>(__cvta_generic_to_shared(smem_raw + kQT * 256));
+  const uint4* sm_code = reinterpret_cast<const uint4*>(smem_raw + kQT * 256);  // kDStages x kQT x 4 chunks
+  const int tid = threadIdx.x;
+
+  auto issue = [&](int64_t tile, int stage) {
+    const int64_t row0 = tile * kQT;
+    const int nrows = static_cast<int>(min(static_cast<int64_t>(kQT), a.n_rows - row0));
+#pragma unroll
+    for (int i = tid; i < kQT * 4; i += kQT) {
+      const int r = i >> 2, c = i & 3;
+      if (r < nrows)
+        cp_async16(code_base + (((stage * kQT + r) * 4 + (c ^ ((r >> 1) & 3))) << 4), a.codes + (row0 + r) * 64 + c * 16);
+    }
+  };
+
+  const int64_t first = blockIdx.x;
+#pragma unroll
+  for (int s = 0; s < kDStages - 1; ++s) {
+    const int64_t t = first + static_cast<int64_t>(s) * gridDim.x;
+    if (t < n_tiles) issue(t, s);
+    cp_async_commit();
+  }
+  for (int64_t k = 0;; ++k) {
+    const int64_t tile = first + k * gridDim.x;
+    if (tile >= n_tiles) break;
+    const int64_t row0 = tile * kQT;
+    const int nrows = static_cast<int>(min(static_cast<int64_t>(kQT), a.n_rows - row0));
+    const int64_t row = row0 + tid;
+    const bool mine = tid < nrows;
+    const bool from_sink = mine && a.sink != nullptr && row < a.sink_rows;
+    // this row's scales (or sink row) are requested before waiting for the codes
+    uint32_t sp[G];
+    uint4 sink_row[16];
+    if (from_sink) {
+#pragma unroll
+      for (int c = 0; c < 16; ++c) sink_row[c] = ld_global_nc_v4(a.sink + row * kQD + c * 8);
+    } else if (mine) {
+      const uint16_t* srow = a.scales + row * G;
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const uint32_t v = __ldg(srow + g);
+        sp[g] = v | (v << 16);
+      }
+    }
+    {
+      const int64_t tn = tile + static_cast<int64_t>(kDStages - 1) * gridDim.x;
+      if (tn < n_tiles) issue(tn, static_cast<int>((k + kDStages - 1) % kDStages));
+      cp_async_commit();
+    }
+    cp_async_wait<kDStages - 1>();
+    __syncthreads();
+    const int stage = static_cast<int>(k % kDStages);
+    uint4* orow = sm_out + tid * 16;
+    if (from_sink) {
+#pragma unroll
+      for (int c = 0; c < 16; ++c) orow[c ^ (tid & 7)] = sink_row[c];
+    } else if (mine) {
+      uint32_t w[16];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const uint4 v = sm_code[(stage * kQT + tid) * 4 + (c ^ ((tid >> 1) & 3))];
+        w[4 * c] = v.x;
+        w[4 * c + 1] = v.y;
+        w[4 * c + 2] = v.z;
+        w[4 * c + 3] = v.w;
+      }
+      deq_row_to<L>(orow, tid, w, sp, std::make_integer_sequence<int, 16>{});
+    }
+    __syncthreads();
+    if (a.rows_contig) {
+      uint4* dst = reinterpret_cast<uint4*>(a.out + row0 * kQD);
+      for (int i = tid; i < nrows * 16; i += kQT) {
+        const int r = i >> 4, c = i & 15;
+        st_global_v4(dst + i, sm_out[r * 16 + (c ^ (r & 7))]);
+      }
+    } else {
+      for (int i = tid; i < nrows * 16; i += kQT) {
+        const int r = i >> 4, c = i & 15;
+        const int64_t rr = row0 + r;
+        const int64_t t = rr / a.H;
+        const int hh = static_cast<int>(rr - t * a.H);
+        st_global_v4(a.out + t * a.out_token_stride + static_cast<int64_t>(hh) * kQD + c * 8,
+                     sm_out[r * 16 + (c ^ (r & 7))]);
+      }
+    }
+    __syncthreads();
+  }
+  cp_async_wait<0>();
+}
+
 static int num_sms() {
   static int sms[64];
   int dev = 0;
@@ -350,15 +565,16 @@ static int num_sms() {
 
 template <class L, int BITS>
 static int launch_fast(const QuantArgs& a, cudaStream_t st) {
-  constexpr int smem = kQT * 256 + kQT * QuantConsts<BITS>::kCodeBytes + ((kQT * L::G * 2 + 15) / 16) * 16;
-  static_assert(smem <= 227 * 1024, "tile too large");
+  constexpr int smem = pipe_smem_bytes<L, BITS>();
+  constexpr int per_sm = (227 * 1024) / smem < 3 ? (227 * 1024) / smem : 3;  // 3 for int4, 2 for int8
+  static_assert(per_sm >= 2, "at least two CTAs per SM must fit");
   // opt in to > 48 KB of dynamic shared memory once per device
   static bool configured[64];
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(quantize_rows_fast<L, BITS>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e = cudaFuncSetAttribute(quantize_rows_pipe<L, BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         smem);
     if (e != cudaSuccess) {
       set_error("cudaFuncSetAttribute(quantize): %s", cudaGetErrorString(e));
       return KVQ_ERR_CUDA;
@@ -366,7 +582,9 @@ static int launch_fast(const QuantArgs& a, cudaStream_t st) {
     configured[dev] = true;
   }
   const int64_t tiles = (a.n_rows + kQT - 1) / kQT;
-  quantize_rows_fast<L, BITS><<<static_cast<unsigned>(tiles), kQT, smem, st>>>(a);
+  const int64_t cap = static_cast<int64_t>(per_sm) * num_sms();
+  const unsigned grid = static_cast<unsigned>(tiles < cap ? tiles : cap);
+  quantize_rows_pipe<L, BITS><<<grid, kQT, smem, st>>>(a, tiles);
   return check_launch("kvq_quantize");
 }
 
@@ -382,6 +600,26 @@ static int dispatch_fast(int layout, const QuantArgs& a, cudaStream_t st) {
   }
   set_error("internal: no specialised kernel for layout %d", layout);
   return KVQ_ERR_UNSUPPORTED;
+}
+
+template <class L>
+static int launch_dequant(const DequantArgs& a, cudaStream_t st) {
+  constexpr int smem = kQT * 256 + kDStages * kQT * 64;
+  static bool configured[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(dequantize_rows_pipe<L>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) {
+      set_error("cudaFuncSetAttribute(dequantize): %s", cudaGetErrorString(e));
+      return KVQ_ERR_CUDA;
+    }
+    configured[dev] = true;
+  }
+  const int64_t tiles = (a.n_rows + kQT - 1) / kQT;
+  const int64_t cap = 3LL * num_sms();
+  dequantize_rows_pipe<L><<<static_cast<unsigned>(tiles < cap ? tiles : cap), kQT, smem, st>>>(a, tiles);
+  return check_launch("kvq_dequantize");
 }
 
 }  // namespace kvq
@@ -465,9 +703,20 @@ extern "C" int kvq_dequantize(const void* codes, const void* scales, const void*
   a.G = n_groups;
   a.bits = bits;
   a.rows_contig = out_token_stride == static_cast<int64_t>(n_heads) * head_dim;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (bits == 4 && layout != kLayoutGeneric && (reinterpret_cast<uintptr_t>(codes) & 15) == 0) {
+    switch (layout) {
+      case kLayoutBands: return launch_dequant<LayoutBands>(a, st);
+      case kLayoutBands2: return launch_dequant<LayoutBands2>(a, st);
+      case kLayoutBands4: return launch_dequant<LayoutBands4>(a, st);
+      case kLayoutBlind32: return launch_dequant<LayoutBlind32>(a, st);
+      case kLayoutBlind64: return launch_dequant<LayoutBlind64>(a, st);
+      default: break;
+    }
+  }
   const int64_t work = a.n_rows * (head_dim / 8);
   const int64_t blocks = (work + 255) / 256;
   const int grid = static_cast<int>(blocks < num_sms() * 16 ? blocks : num_sms() * 16);
-  dequantize_rows<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(a, map);
+  dequantize_rows<<<grid, 256, 0, st>>>(a, map);
   return check_launch("kvq_dequantize");
 }

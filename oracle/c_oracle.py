@@ -36,6 +36,11 @@ def lib():
         L.kvqo_check_fast_codes.argtypes = [i32, ctypes.c_float, i32,
                                             ctypes.POINTER(ctypes.c_uint32)]
         L.kvqo_check_fast_codes.restype = ctypes.c_longlong
+        L.kvqo_check_fast_codes_rcp.argtypes = [i32, ctypes.c_float, i32, i32,
+                                                ctypes.POINTER(ctypes.c_uint32)]
+        L.kvqo_check_fast_codes_rcp.restype = ctypes.c_longlong
+        L.kvqo_check_scale_div.argtypes = [i32]
+        L.kvqo_check_scale_div.restype = ctypes.c_longlong
         _lib = L
     return _lib
 
@@ -88,3 +93,18 @@ def check_fast_codes(qmax: int, exact_below: float, threads: int | None = None):
     n = lib().kvqo_check_fast_codes(qmax, exact_below, threads or os.cpu_count() or 1,
                                     ctypes.byref(first))
     return int(n), (first.value >> 16, first.value & 0xFFFF)
+
+
+def check_fast_codes_any_rcp(qmax: int, exact_below: float, threads: int | None = None):
+    """As check_fast_codes, but the formula must hold for every reciprocal within
+    one ulp of 1/s."""
+    first = ctypes.c_uint32()
+    n = lib().kvqo_check_fast_codes_rcp(qmax, exact_below, 1, threads or os.cpu_count() or 1,
+                                        ctypes.byref(first))
+    return int(n), (first.value >> 16, first.value & 0xFFFF)
+
+
+def check_scale_div(qmax: int) -> int:
+    """Exhaustive count of bf16 amax where the kernel's divide-free group scale
+    differs from the IEEE quotient amax / qmax."""
+    return int(lib().kvqo_check_scale_div(qmax))

@@ -186,6 +186,7 @@ typedef struct {
   int qmax;
   uint32_t a0, a1; /* amax bit-pattern range (positive finite bf16) */
   float exact_below;
+  int any_rcp;
   long long mismatches;
   uint32_t first;
 } xjob_t;
@@ -205,7 +206,19 @@ static void* exhaustive_thread(void* p) {
       float ref = nearbyintf(x / s);
       if (ref > j->qmax) ref = (float)j->qmax;
       float got;
-      if (fast) {
+      if (fast && j->any_rcp) {
+        /* the same with each reciprocal within 1 ulp of 1/s: RN(1/s) and both
+         * neighbours; a mismatch for any of them counts */
+        const float rs[3] = {r, nextafterf(r, 0.0f), nextafterf(r, INFINITY)};
+        got = ref;
+        for (int k = 0; k < 3; ++k) {
+          float y0 = x * rs[k];
+          float rem = fmaf(-y0, s, x);
+          float g = nearbyintf(fmaf(rem, rs[k], y0));
+          if (g > j->qmax) g = (float)j->qmax;
+          if (g != ref) got = g;
+        }
+      } else if (fast) {
         /* Markstein refinement: y0 = RN(x*r), rem = x - y0*s exactly (FMA),
          * y1 = RN(y0 + rem*r) = RN(x/s) when r = RN(1/s). */
         float y0 = x * r;
@@ -224,7 +237,15 @@ static void* exhaustive_thread(void* p) {
   return NULL;
 }
 
+long long kvqo_check_fast_codes_rcp(int qmax, float exact_below, int any_rcp, int threads, uint32_t* first);
 long long kvqo_check_fast_codes(int qmax, float exact_below, int threads, uint32_t* first) {
+  return kvqo_check_fast_codes_rcp(qmax, exact_below, 0, threads, first);
+}
+
+/* any_rcp != 0: the per-element formula must hold for every reciprocal within
+ * one ulp of 1/s (RN(1/s) and its two neighbours), so an approximate reciprocal
+ * refined to 1-ulp accuracy may be used. */
+long long kvqo_check_fast_codes_rcp(int qmax, float exact_below, int any_rcp, int threads, uint32_t* first) {
   if (threads < 1) threads = 1;
   if (threads > 64) threads = 64;
   xjob_t jobs[64];
@@ -237,6 +258,7 @@ long long kvqo_check_fast_codes(int qmax, float exact_below, int threads, uint32
     jobs[i].a0 = (uint32_t)(f0 * top);
     jobs[i].a1 = (i == threads - 1) ? top : (uint32_t)(f1 * top);
     jobs[i].exact_below = exact_below;
+    jobs[i].any_rcp = any_rcp;
   }
   for (int i = 0; i < threads; ++i) pthread_create(&tid[i], NULL, exhaustive_thread, &jobs[i]);
   long long total = 0;
@@ -248,4 +270,24 @@ long long kvqo_check_fast_codes(int qmax, float exact_below, int threads, uint32
   }
   if (first) *first = f;
   return total;
+}
+
+/* ------------------------------------------------------------------------- exhaustive check
+ * Group scale without a divide: the kernel computes s = amax / qmax as
+ *   r = RN(1/qmax), q0 = RN(amax * r), rem = RN(amax - q0 * qmax) (FMA),
+ *   s = RN(q0 + rem * r) (FMA)
+ * and this returns the number of positive finite bf16 amax for which that
+ * differs from the IEEE quotient RN(amax / qmax) (quant_kv.py:151). */
+long long kvqo_check_scale_div(int qmax) {
+  const float r = 1.0f / (float)qmax;
+  long long bad = 0;
+  for (uint32_t ab = 1; ab < 0x7F80u; ++ab) {
+    float amax = bf16_to_f32((uint16_t)ab);
+    float ref = amax / (float)qmax;
+    float q0 = amax * r;
+    float rem = fmaf(-q0, (float)qmax, amax);
+    float s = fmaf(rem, r, q0);
+    if (s != ref) bad++;
+  }
+  return bad;
 }

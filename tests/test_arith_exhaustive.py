@@ -25,3 +25,18 @@ def test_plain_reciprocal_is_not_exact():
     # guard (and the check itself) is doing work.
     n, _ = c_oracle.check_fast_codes(7, 0.0)
     assert n > 0
+
+
+def test_group_scale_without_divide_is_exact():
+    # s = fma(fma(-amax*r, qmax, amax), r, amax*r), r = RN(1/qmax), equals the
+    # IEEE amax / qmax for every positive finite bf16 amax
+    assert c_oracle.check_scale_div(7) == 0
+    assert c_oracle.check_scale_div(127) == 0
+
+
+def test_fast_code_formula_holds_for_any_one_ulp_reciprocal():
+    # the kernel's reciprocal is an approximation refined by one Newton step,
+    # within one ulp of 1/s: the formula must hold for RN(1/s) and both neighbours
+    for qmax in (7, 127):
+        n, first = c_oracle.check_fast_codes_any_rcp(qmax, 2.0 ** -100)
+        assert n == 0, f"qmax {qmax}: {n} mismatches, first {first}"
