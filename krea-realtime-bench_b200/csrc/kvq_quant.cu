@@ -103,9 +103,9 @@ __device__ __forceinline__ float group_scale(float amax) {
 // the second and keep the other three
 __device__ constexpr uint32_t kInsertByte[4] = {0x3214u, 0x3240u, 0x3410u, 0x4210u};
 
-template <int LO, int HI, int BITS>
+template <int LO, int HI, int BITS, int G_INDEX>
 __device__ __forceinline__ void quant_group(const uint32_t (&w)[64], uint32_t (&ow)[BITS == 4 ? 16 : 32],
-                                            uint16_t& scale_out) {
+                                            uint16_t& scale_out, uint32_t& slow_mask) {
   using C = QuantConsts<BITS>;
   static_assert(LO % 2 == 0 && HI % 2 == 0 && LO < HI, "groups must start and end on even channels");
   uint32_t m = 0;
@@ -120,53 +120,89 @@ __device__ __forceinline__ void quant_group(const uint32_t (&w)[64], uint32_t (&
   float s = group_scale<C::kQmax>(amax);
   s = (s > 0.0f) ? s : 1.0f;  // quant_kv.py:152 (also maps NaN to 1, like torch.where)
   scale_out = f32_to_bf16_bits(s);
-  const bool fast = (amax >= 0x1p-100f) && (amax <= 3.0e38f);
-  if (fast) {
-    // reciprocal within one ulp of 1/s: hardware approximation + one Newton step
-    // (the code formula holds for any such r, kvqo_check_fast_codes_rcp)
-    float r;
-    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(s));
-    r = __fmaf_rn(r, __fmaf_rn(-s, r, 1.0f), r);
-    // the per-element chain on packed f32x2: two channels per instruction
-    const float2 r2 = make_float2(r, r), ns2 = make_float2(-s, -s);
-    const float2 mg2 = make_float2(C::kMagic, C::kMagic);
+  // groups with a tiny or non-finite amax are recomputed with the IEEE divide by
+  // quant_fix_slow after staging; the fast chain below still runs for them (any
+  // value it produces is overwritten)
+  if (!((amax >= 0x1p-100f) && (amax <= 3.0e38f))) slow_mask |= 1u << G_INDEX;
+  // reciprocal within one ulp of 1/s: hardware approximation + one Newton step
+  // (the code formula holds for any such r, kvqo_check_fast_codes_rcp)
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(s));
+  r = __fmaf_rn(r, __fmaf_rn(-s, r, 1.0f), r);
+  // the per-element chain on packed f32x2: two channels per instruction
+  const float2 r2 = make_float2(r, r), ns2 = make_float2(-s, -s);
+  const float2 mg2 = make_float2(C::kMagic, C::kMagic);
 #pragma unroll
-    for (int k = LO / 2; k < HI / 2; ++k) {
-      const float2 x = make_float2(bf16lo_to_f32(w[k]), bf16hi_to_f32(w[k]));
-      const float2 y0 = __fmul2_rn(x, r2);
-      const float2 rem = __ffma2_rn(y0, ns2, x);
-      const float2 t = __fadd2_rn(__ffma2_rn(rem, r2, y0), mg2);
-      const uint32_t c0 = __float_as_uint(t.x), c1 = __float_as_uint(t.y);
-      if constexpr (BITS == 4) {
-        // low byte of c0 + 16 * c1 is the packed pair (code bytes are < 16)
-        const uint32_t pair = c0 + (c1 << 4);
-        ow[k >> 2] = __byte_perm(ow[k >> 2], pair, kInsertByte[k & 3]);
-      } else {
-        const uint32_t half = __byte_perm(c0, c1, 0x0040);
-        ow[k >> 1] = __byte_perm(ow[k >> 1], half, (k & 1) ? 0x5410u : 0x3254u);
-      }
-    }
-  } else {
-    const float q = static_cast<float>(C::kQmax);
-#pragma unroll
-    for (int k = LO / 2; k < HI / 2; ++k) {
-      uint32_t c0 = code_exact(bf16lo_to_f32(w[k]), s, q, C::kMagic);
-      uint32_t c1 = code_exact(bf16hi_to_f32(w[k]), s, q, C::kMagic);
-      if constexpr (BITS == 4) {
-        uint32_t byte = (c0 & 0xFu) | ((c1 & 0xFu) << 4);
-        ow[k >> 2] |= byte << (8 * (k & 3));
-      } else {
-        uint32_t half = (c0 & 0xFFu) | ((c1 & 0xFFu) << 8);
-        ow[k >> 1] |= half << (16 * (k & 1));
-      }
+  for (int k = LO / 2; k < HI / 2; ++k) {
+    const float2 x = make_float2(bf16lo_to_f32(w[k]), bf16hi_to_f32(w[k]));
+    const float2 y0 = __fmul2_rn(x, r2);
+    const float2 rem = __ffma2_rn(y0, ns2, x);
+    const float2 t = __fadd2_rn(__ffma2_rn(rem, r2, y0), mg2);
+    const uint32_t c0 = __float_as_uint(t.x), c1 = __float_as_uint(t.y);
+    if constexpr (BITS == 4) {
+      // low byte of c0 + 16 * c1 is the packed pair (code bytes are < 16)
+      const uint32_t pair = c0 + (c1 << 4);
+      ow[k >> 2] = __byte_perm(ow[k >> 2], pair, kInsertByte[k & 3]);
+    } else {
+      const uint32_t half = __byte_perm(c0, c1, 0x0040);
+      ow[k >> 1] = __byte_perm(ow[k >> 1], half, (k & 1) ? 0x5410u : 0x3254u);
     }
   }
 }
 
 template <class L, int BITS, int... Gs>
 __device__ __forceinline__ void quant_row(const uint32_t (&w)[64], uint32_t (&ow)[BITS == 4 ? 16 : 32],
-                                          uint16_t (&sc)[L::G], std::integer_sequence<int, Gs...>) {
-  (quant_group<L::E[Gs], L::E[Gs + 1], BITS>(w, ow, sc[Gs]), ...);
+                                          uint16_t (&sc)[L::G], uint32_t& slow_mask,
+                                          std::integer_sequence<int, Gs...>) {
+  (quant_group<L::E[Gs], L::E[Gs + 1], BITS, Gs>(w, ow, sc[Gs], slow_mask), ...);
+}
+
+template <class L, int... Is>
+__device__ __forceinline__ void fill_edges(int (&e)[L::G + 1], std::integer_sequence<int, Is...>) {
+  ((e[Is] = std::integral_constant<int, L::E[Is]>::value), ...);
+}
+
+// Rare path: recomputes the codes of the groups flagged in slow_mask (amax below
+// 2^-100 or not finite) with the reference formula, IEEE divide and clamp, from
+// the row in the swizzled input stage, and patches the staged codes.
+template <int BITS>
+__device__ __noinline__ void quant_fix_slow(const uint4* tin_row, int r, uint32_t slow_mask, const int* edges,
+                                            const uint16_t* scales_row, uint4* codes_row) {
+  using C = QuantConsts<BITS>;
+  const float q = static_cast<float>(C::kQmax);
+  const uint16_t* xr = reinterpret_cast<const uint16_t*>(tin_row);
+  uint8_t* cb = reinterpret_cast<uint8_t*>(codes_row);
+  for (int g = 0; slow_mask; ++g, slow_mask >>= 1) {
+    if (!(slow_mask & 1u)) continue;
+    // the unrounded fp32 scale of the group, as the main path computed it
+    float amax = 0.0f;
+    bool nan = false;
+    for (int c = edges[g]; c < edges[g + 1]; ++c) {
+      const int chunk = c >> 3, e = c & 7;
+      const float x = bf16_bits_to_f32(xr[((chunk ^ (r & 7)) << 3) + e]);
+      nan |= (x != x);
+      amax = fmaxf(amax, fabsf(x));
+    }
+    if (nan) amax = __uint_as_float(0x7FC00000u);
+    float s = __fdiv_rn(amax, q);
+    s = (s > 0.0f) ? s : 1.0f;
+    for (int c = edges[g]; c < edges[g + 1]; ++c) {
+      const int chunk = c >> 3, e = c & 7;
+      const float x = bf16_bits_to_f32(xr[((chunk ^ (r & 7)) << 3) + e]);
+      const uint32_t code = code_exact(x, s, q, C::kMagic) & 0xFFu;
+      if constexpr (BITS == 4) {
+        const int byte = c >> 1, chunk16 = byte >> 4;
+        const int slot = chunk16 ^ ((r >> 1) & 3);
+        uint8_t& b = cb[(slot << 4) + (byte & 15)];
+        b = (c & 1) ? static_cast<uint8_t>((b & 0x0F) | (code << 4)) : static_cast<uint8_t>((b & 0xF0) | code);
+      } else {
+        const int chunk16 = c >> 4;
+        const int slot = chunk16 ^ (r & 7);
+        cb[(slot << 4) + (c & 15)] = static_cast<uint8_t>(code);
+      }
+    }
+    (void)scales_row;
+  }
 }
 
 __device__ __forceinline__ void cp_async16(uint32_t dst_smem, const void* src) {
@@ -253,7 +289,8 @@ __global__ void __launch_bounds__(kQT, 3) quantize_rows_pipe(QuantArgs a, int64_
 #pragma unroll
       for (int q = 0; q < (BITS == 4 ? 16 : 32); ++q) ow[q] = 0;
       uint16_t sc[G];
-      quant_row<L, BITS>(w, ow, sc, std::make_integer_sequence<int, G>{});
+      uint32_t slow_mask = 0;
+      quant_row<L, BITS>(w, ow, sc, slow_mask, std::make_integer_sequence<int, G>{});
 #pragma unroll
       for (int c = 0; c < CCH; ++c) {
         const int slot = (BITS == 4) ? (c ^ ((tid >> 1) & 3)) : (c ^ (tid & 7));
@@ -261,6 +298,11 @@ __global__ void __launch_bounds__(kQT, 3) quantize_rows_pipe(QuantArgs a, int64_
       }
 #pragma unroll
       for (int g = 0; g < G; ++g) sm_sc[tid * G + g] = sc[g];
+      if (slow_mask) {
+        int edges[G + 1];
+        fill_edges<L>(edges, std::make_integer_sequence<int, G + 1>{});
+        quant_fix_slow<BITS>(tin + tid * 16, tid, slow_mask, edges, sm_sc + tid * G, sm_codes + tid * CCH);
+      }
     }
     __syncthreads();
     {
