@@ -11,9 +11,11 @@
 // every dequantized K/V tile. 512 threads, warp-specialised:
 //   warps 0-3 / 4-7  softmax for Q tile 0 / 1: thread r owns Q row r (TMEM lane
 //                    r). Loads its Q row into TMEM once; per KV tile reads S
-//                    (64 columns) from TMEM, online base-2 softmax with lazy
-//                    rescaling of O (only when the row max grows by > 2^8),
-//                    writes P as bf16 back into TMEM over S; finally normalises O.
+//                    (64 columns) from TMEM and frees the S buffer at once, online
+//                    base-2 softmax with lazy rescaling of O (only when the row
+//                    max grows by > 2^8), writes P as bf16 into a shared-memory
+//                    tile (double-buffered, 128B-swizzled K-major); finally
+//                    normalises O.
 //   warps 8-11       converters: per KV tile of 64 tokens, warps 8-9 dequantize
 //                    the K rows and 10-11 the V rows (one row per thread) from
 //                    the TMA-staged codes into 128B-swizzled bf16 tiles, with
@@ -21,12 +23,25 @@
 //   warp 12          TMA producer: packed codes (SWIZZLE_64B staging) and, for
 //                    tiles that reach into the sink, the bf16 sink rows straight
 //                    into the bf16 tiles (SWIZZLE_128B, the MMA's layout).
-//   warp 13          TMEM allocation (512 columns) and the thread issuing
-//                    tcgen05.mma with A in TMEM: S_x = Q_x K^T (M=128, N=64,
-//                    K=128) and O_x += P_x V (M=128, N=128, K=64), V read as an
-//                    MN-major shared-memory operand.
+//   warps 13 / 14    one thread each issuing the tcgen05.mma of Q tile 0 / 1:
+//                    S_x = Q_x K^T (M=128, N=64, K=128, Q in TMEM) and O_x +=
+//                    P_x V (M=128, N=128, K=64, P and V in shared memory, V
+//                    MN-major). Warp 13 also owns the TMEM allocation.
+// Pipelining (measured on B200, drives the layout):
+//  - P does not live in the S buffer, so S_x(j+1) is issued as soon as the
+//    softmax has loaded S_x(j) into registers and completes while the softmax
+//    of tile j still runs: the softmax warps go from one KV tile to the next
+//    without waiting for a PV -> S round trip of the tensor pipe.
+//  - One issuing thread per Q tile: a single thread issues a tcgen05.mma only
+//    every ~60-100 cycles and blocks ~250 cycles on each tcgen05.commit, which
+//    leaves the tensor pipe half idle; two threads keep it fed.
+//  - One commit per KV tile and thread (S_x full). Everything else is derived
+//    from it, since one thread's MMAs complete in issue order (S_x(j) is
+//    issued behind PV_x(j-2)): the softmax that sees S_x(j) releases K/V stage
+//    j-2 and may reuse P buffer j & 1; a rescale of O at tile j waits for
+//    S_x(j+1), i.e. for PV_x(j-1).
 // TMEM columns: Q_0 [0,64) Q_1 [64,128) (bf16 pairs), O_0 [128,256) O_1
-// [256,384), S_0 [384,448) S_1 [448,512) (P_x over the first 32 of S_x).
+// [256,384), S_0 [384,448) S_1 [448,512).
 // Synchronisation is by mbarriers with one arrival per warp; every wait gives up
 // after about a second, raising the device status word (kvq_device_status()).
 #include <cuda.h>
@@ -48,10 +63,10 @@ namespace attn {
 constexpr int BM = 128;   // rows per Q tile
 constexpr int BN = 64;    // KV tokens per tile
 constexpr int D = 128;
-constexpr int NS_KV = 3;  // bf16 K/V tile stages
+constexpr int NS_KV = 4;  // bf16 K/V tile stages
 constexpr int NS_LD = 4;  // packed-code stages
 constexpr int kThreads = 16 * 32;
-constexpr int kConvWarp0 = 8, kProdWarp = 12, kMmaWarp = 13;
+constexpr int kConvWarp0 = 8, kProdWarp = 12, kMmaWarp = 13;  // MMA issuers: warps 13 (Q tile 0), 14 (Q tile 1)
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColQ = 0, kColO = 128, kColS = 384;
 
@@ -62,11 +77,14 @@ constexpr int kOffK = 0;
 constexpr int kOffV = kOffK + NS_KV * kKVTile;
 constexpr int kOffKC = kOffV + NS_KV * kKVTile;
 constexpr int kOffVC = kOffKC + NS_LD * kCodeTile;
-constexpr int kOffBar = kOffVC + NS_LD * kCodeTile;
+constexpr int kPTile = BM * BN * 2;  // 16 KB: P_x, 128 rows x 128 B, one SWIZZLE_128B atom column
+constexpr int kOffP = kOffVC + NS_LD * kCodeTile;
+constexpr int kOffBar = kOffP + 4 * kPTile;  // P_x buffer u at kOffP + (2x + u) * kPTile
 // barrier indices
 constexpr int bLdFull = 0, bLdEmpty = bLdFull + NS_LD, bKvFull = bLdEmpty + NS_LD, bKvEmpty = bKvFull + NS_KV,
-              bQReady = bKvEmpty + NS_KV, bSFull = bQReady + 2, bPFull = bSFull + 2, bOFinal = bPFull + 2,
-              bMmaDone = bOFinal + 2, kNumBars = bMmaDone + 1;
+              bQReady = bKvEmpty + NS_KV, bSFull = bQReady + 2, bSFree = bSFull + 2, bPFull = bSFree + 2,
+              bOReady = bPFull + 4, bOFinal = bOReady + 2, bMmaDone = bOFinal + 2, kNumBars = bMmaDone + 2;
+static_assert(kOffP % 1024 == 0, "SWIZZLE_128B operands need 1024-byte alignment");
 constexpr int kOffMisc = kOffBar + kNumBars * 8;
 constexpr int kSmemBytes = kOffMisc + 64 + 1024;  // + alignment slack
 
@@ -213,15 +231,19 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
     }
     for (int i = 0; i < NS_KV; ++i) {
       mbar_init(&bars[bKvFull + i], 4);
-      mbar_init(&bars[bKvEmpty + i], 1);
+      mbar_init(&bars[bKvEmpty + i], 2);  // one arrival per Q tile (softmax warp 4x)
     }
     for (int x = 0; x < 2; ++x) {
       mbar_init(&bars[bQReady + x], 4);
       mbar_init(&bars[bSFull + x], 1);
-      mbar_init(&bars[bPFull + x], 4);
+      mbar_init(&bars[bSFree + x], 4);
+      mbar_init(&bars[bPFull + 2 * x], 4);
+      mbar_init(&bars[bPFull + 2 * x + 1], 4);
+      mbar_init(&bars[bOReady + x], 1);
       mbar_init(&bars[bOFinal + x], 1);
     }
     mbar_init(&bars[bMmaDone], 1);
+    mbar_init(&bars[bMmaDone + 1], 1);
     *abort = 0;
     fence_mbar_init();
   }
@@ -282,9 +304,15 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
         ok = false;
         break;
       }
+      // S_x(j) complete => PV_x(j-2) complete: this Q tile no longer reads stage j-2
+      if (j >= 2 && (warp & 3) == 0 && lane == 0) mbar_arrive(&bars[bKvEmpty + (j - 2) % NS_KV]);
       tc_fence_after();
       uint32_t s0[32], s1[32];
       tmem_ld32x2_wait(tS, tS + 32, s0, s1);
+      // S_x(j) is in registers: the MMA may overwrite the buffer with S_x(j+1)
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[bSFree + x]);
       const int valid = min(BN, a.Lk - j * BN);
       float mx = -INFINITY;
       if (valid == BN) {
@@ -309,7 +337,17 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
         l *= alpha;
       }
       if (__any_sync(0xffffffffu, rescale)) {
-        // O_x is complete up to PV_x(j-1): S_x(j) was issued after it
+        // O_x must hold every product up to PV_x(j-1) before it is rescaled:
+        // wait for S_x(j+1), issued behind PV_x(j-1) (S_x(j+2) needs this
+        // tile's next S-free, so the phase seen next step is still j+1), or,
+        // at the last tile, for the commit that follows PV_x(j-1).
+        const bool last = j + 1 == nkv;
+        if (!mbar_wait_warp(&bars[last ? bOReady + x : bSFull + x], last ? 0u : static_cast<uint32_t>((j + 1) & 1),
+                            abort, &g_attn_status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
 #pragma unroll 1
         for (int k = 0; k < 4; ++k) {
           uint32_t o[32];
@@ -318,6 +356,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
           for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
           tmem_st32(tO + 32 * k, o);
         }
+        tmem_wait_st();
       }
       const float nm = -m;
       float sum = 0.0f;
@@ -339,11 +378,16 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
         pw[16 + c] = pack_bf16x2(p2, p3);
       }
       l += sum;
-      tmem_st32(tS, pw);  // P_x(j), 64 bf16 = 32 columns, over S_x(j)
-      tmem_wait_st();
-      tc_fence_before();
+      // P_x(j) -> buffer j & 1, row r, K-major SWIZZLE_128B. The buffer was last
+      // read by PV_x(j-2), which completed before S_x(j) (issued behind it).
+      const uint32_t pdst = sbase + kOffP + (2 * x + (j & 1)) * kPTile + r * 128;
+#pragma unroll
+      for (int c = 0; c < 8; ++c)
+        st_shared_v4(pdst + ((c ^ (r & 7)) << 4), make_uint4(pw[4 * c], pw[4 * c + 1], pw[4 * c + 2], pw[4 * c + 3]));
+      fence_proxy_async_smem();
+      tc_fence_before();  // orders a rescale's TMEM stores before PV_x(j)
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bars[bPFull + x]);
+      if (lane == 0) mbar_arrive(&bars[bPFull + 2 * x + (j & 1)]);
     }
     if (ok && mbar_wait_warp(&bars[bOFinal + x], 0, abort, &g_attn_status)) {
       tc_fence_after();
@@ -441,58 +485,54 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
       }
     }
     __syncwarp();
-  } else if (warp == kMmaWarp) {
-    // ------------------------------------------------------------ MMA issuer
+  } else if (warp == kMmaWarp || warp == kMmaWarp + 1) {
+    // ------------------------------------------------------------ MMA issuers
+    const int x = warp - kMmaWarp;
     if (lane == 0) {
       constexpr uint32_t idS = idesc_bf16(BM, BN, 0);
       constexpr uint32_t idPV = idesc_bf16(BM, D, 1);
-      auto issue_s = [&](int x, int j) {
+      const uint32_t tS = tmem + kColS + 64 * x, tQ = tmem + kColQ + 64 * x, tO = tmem + kColO + 128 * x;
+      auto issue_s = [&](int j) {
         const uint32_t kaddr = sbase + kOffK + (j % NS_KV) * kKVTile;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          mma_bf16_ts(tmem + kColS + 64 * x, tmem + kColQ + 64 * x + 8 * kk,
-                      smem_desc_sw128(kaddr + (kk >> 2) * kAtom + (kk & 3) * 32, 16, 1024), idS, kk > 0);
+          mma_bf16_ts(tS, tQ + 8 * kk, smem_desc_sw128(kaddr + (kk >> 2) * kAtom + (kk & 3) * 32, 16, 1024), idS,
+                      kk > 0);
         mma_commit(&bars[bSFull + x]);
       };
-      auto issue_pv = [&](int x, int j) {
+      // O_x += P_x(j) V(j): P K-major from buffer j & 1, V MN-major
+      auto issue_pv = [&](int j) {
         const uint32_t vaddr = sbase + kOffV + (j % NS_KV) * kKVTile;
+        const uint32_t paddr = sbase + kOffP + (2 * x + (j & 1)) * kPTile;
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk)
-          mma_bf16_ts(tmem + kColO + 128 * x, tmem + kColS + 64 * x + 8 * kk,
-                      smem_desc_sw128(vaddr + kk * 2048, kAtom, 1024), idPV, (j > 0 || kk > 0) ? 1u : 0u);
+          mma_bf16_ss(tO, smem_desc_sw128(paddr + kk * 32, 16, 1024), smem_desc_sw128(vaddr + kk * 2048, kAtom, 1024),
+                      idPV, (j > 0 || kk > 0) ? 1u : 0u);
       };
-      bool ok = mbar_wait(&bars[bQReady + 0], 0, abort, &g_attn_status) &&
-                mbar_wait(&bars[bQReady + 1], 0, abort, &g_attn_status) &&
-                mbar_wait(&bars[bKvFull + 0], 0, abort, &g_attn_status);
+      auto wait_kv = [&](int j) {
+        return mbar_wait(&bars[bKvFull + j % NS_KV], (j / NS_KV) & 1, abort, &g_attn_status);
+      };
+      bool ok = mbar_wait(&bars[bQReady + x], 0, abort, &g_attn_status) && wait_kv(0);
       if (ok) {
         tc_fence_after();
-        issue_s(0, 0);
-        issue_s(1, 0);
+        issue_s(0);
       }
       for (int j = 0; j < nkv && ok; ++j) {
-        if (!(ok = mbar_wait(&bars[bPFull + 0], j & 1, abort, &g_attn_status))) break;
-        tc_fence_after();
-        issue_pv(0, j);
-        const bool more = j + 1 < nkv;
-        if (more) {
-          if (!(ok = mbar_wait(&bars[bKvFull + (j + 1) % NS_KV], ((j + 1) / NS_KV) & 1, abort, &g_attn_status)))
-            break;
+        if (j + 1 < nkv) {
+          // S_x(j+1) as soon as the softmax has taken S_x(j) out of TMEM
+          if (!(ok = wait_kv(j + 1) && mbar_wait(&bars[bSFree + x], j & 1, abort, &g_attn_status))) break;
           tc_fence_after();
-          issue_s(0, j + 1);
+          issue_s(j + 1);
         }
-        if (!(ok = mbar_wait(&bars[bPFull + 1], j & 1, abort, &g_attn_status))) break;
+        if (!(ok = mbar_wait(&bars[bPFull + 2 * x + (j & 1)], (j >> 1) & 1, abort, &g_attn_status))) break;
         tc_fence_after();
-        issue_pv(1, j);
-        mma_commit(&bars[bKvEmpty + j % NS_KV]);
-        if (more) issue_s(1, j + 1);
+        issue_pv(j);
+        if (j + 2 == nkv) mma_commit(&bars[bOReady + x]);  // PV_x(nkv-2): a rescale at the last tile waits for it
       }
-      if (ok) {
-        mma_commit(&bars[bOFinal + 0]);
-        mma_commit(&bars[bOFinal + 1]);
-      }
+      if (ok) mma_commit(&bars[bOFinal + x]);
       // all MMAs issued by this thread have completed before TMEM is released
-      mma_commit(&bars[bMmaDone]);
-      mbar_wait(&bars[bMmaDone], 0, abort, &g_attn_status);
+      mma_commit(&bars[bMmaDone + x]);
+      mbar_wait(&bars[bMmaDone + x], 0, abort, &g_attn_status);
     }
     __syncwarp();
   }
