@@ -10,12 +10,11 @@
 // One CTA per (pair of 128-row Q tiles, head, stream); the two Q tiles share
 // every dequantized K/V tile. 512 threads, warp-specialised:
 //   warps 0-3 / 4-7  softmax for Q tile 0 / 1: thread r owns Q row r (TMEM lane
-//                    r). Loads its Q row into TMEM once; per KV tile reads S
-//                    (64 columns) from TMEM and frees the S buffer at once, online
-//                    base-2 softmax with lazy rescaling of O (only when the row
-//                    max grows by > 2^8), writes P as bf16 into a shared-memory
-//                    tile (double-buffered, 128B-swizzled K-major); finally
-//                    normalises O.
+//                    r). Stores its Q row into shared memory once (the MMA's
+//                    128B-swizzled K-major layout); per KV tile reads S (64
+//                    columns) from TMEM, online base-2 softmax with lazy
+//                    rescaling of O (only when the row max grows by > 2^8),
+//                    writes P as bf16 back into TMEM over S; finally normalises O.
 //   warps 8-11       converters: per KV tile of 64 tokens, warps 8-9 dequantize
 //                    the K rows and 10-11 the V rows (one row per thread) from
 //                    the TMA-staged codes into 128B-swizzled bf16 tiles, with
@@ -24,24 +23,25 @@
 //                    tiles that reach into the sink, the bf16 sink rows straight
 //                    into the bf16 tiles (SWIZZLE_128B, the MMA's layout).
 //   warps 13 / 14    one thread each issuing the tcgen05.mma of Q tile 0 / 1:
-//                    S_x = Q_x K^T (M=128, N=64, K=128, Q in TMEM) and O_x +=
-//                    P_x V (M=128, N=128, K=64, P and V in shared memory, V
-//                    MN-major). Warp 13 also owns the TMEM allocation.
+//                    S_x = Q_x K^T (M=128, N=64, K=128, Q and K in shared
+//                    memory) and O_x += P_x V (M=128, N=128, K=64, P in TMEM, V
+//                    an MN-major shared-memory operand). Warp 13 also owns the
+//                    TMEM allocation.
 // Pipelining (measured on B200, drives the layout):
-//  - P does not live in the S buffer, so S_x(j+1) is issued as soon as the
-//    softmax has loaded S_x(j) into registers and completes while the softmax
-//    of tile j still runs: the softmax warps go from one KV tile to the next
-//    without waiting for a PV -> S round trip of the tensor pipe.
+//  - S is double-buffered per Q tile and S_x(j+2) is issued right behind
+//    PV_x(j) (one thread's MMAs run in issue order, so it overwrites P_x(j)
+//    only after PV_x(j) has read it): S_x(j+1) has a whole softmax step to
+//    complete and the softmax warps go from one KV tile to the next without
+//    waiting for the tensor pipe or for a straggling warp of their Q tile.
 //  - One issuing thread per Q tile: a single thread issues a tcgen05.mma only
 //    every ~60-100 cycles and blocks ~250 cycles on each tcgen05.commit, which
 //    leaves the tensor pipe half idle; two threads keep it fed.
 //  - One commit per KV tile and thread (S_x full). Everything else is derived
-//    from it, since one thread's MMAs complete in issue order (S_x(j) is
-//    issued behind PV_x(j-2)): the softmax that sees S_x(j) releases K/V stage
-//    j-2 and may reuse P buffer j & 1; a rescale of O at tile j waits for
-//    S_x(j+1), i.e. for PV_x(j-1).
-// TMEM columns: Q_0 [0,64) Q_1 [64,128) (bf16 pairs), O_0 [128,256) O_1
-// [256,384), S_0 [384,448) S_1 [448,512).
+//    from it: the softmax that sees S_x(j) (issued behind PV_x(j-2)) releases
+//    K/V stage j-2; a rescale of O at tile j waits for S_x(j+1) (issued behind
+//    PV_x(j-1)).
+// TMEM columns: O_0 [0,128) O_1 [128,256), S_0 [256,320) [320,384), S_1
+// [384,448) [448,512) (P over the first 32 columns of its S buffer).
 // Synchronisation is by mbarriers with one arrival per warp; every wait gives up
 // after about a second, raising the device status word (kvq_device_status()).
 #include <cuda.h>
@@ -68,7 +68,7 @@ constexpr int NS_LD = 4;  // packed-code stages
 constexpr int kThreads = 16 * 32;
 constexpr int kConvWarp0 = 8, kProdWarp = 12, kMmaWarp = 13;  // MMA issuers: warps 13 (Q tile 0), 14 (Q tile 1)
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColQ = 0, kColO = 128, kColS = 384;
+constexpr uint32_t kColO = 0, kColS = 256;  // S_x buffer u at kColS + 128x + 64u
 
 constexpr int kKVTile = BN * D * 2;     // 16 KB: two 8 KB SWIZZLE_128B atoms (d 0-63, 64-127)
 constexpr int kAtom = BN * 128;         // 8 KB
@@ -77,14 +77,15 @@ constexpr int kOffK = 0;
 constexpr int kOffV = kOffK + NS_KV * kKVTile;
 constexpr int kOffKC = kOffV + NS_KV * kKVTile;
 constexpr int kOffVC = kOffKC + NS_LD * kCodeTile;
-constexpr int kPTile = BM * BN * 2;  // 16 KB: P_x, 128 rows x 128 B, one SWIZZLE_128B atom column
-constexpr int kOffP = kOffVC + NS_LD * kCodeTile;
-constexpr int kOffBar = kOffP + 4 * kPTile;  // P_x buffer u at kOffP + (2x + u) * kPTile
+constexpr int kQTile = BM * D * 2;  // 32 KB: Q_x as two 16 KB SWIZZLE_128B atoms (d 0-63, 64-127)
+constexpr int kQAtom = BM * 128;    // 16 KB
+constexpr int kOffQ = kOffVC + NS_LD * kCodeTile;
+constexpr int kOffBar = kOffQ + 2 * kQTile;
 // barrier indices
 constexpr int bLdFull = 0, bLdEmpty = bLdFull + NS_LD, bKvFull = bLdEmpty + NS_LD, bKvEmpty = bKvFull + NS_KV,
-              bQReady = bKvEmpty + NS_KV, bSFull = bQReady + 2, bSFree = bSFull + 2, bPFull = bSFree + 2,
-              bOReady = bPFull + 4, bOFinal = bOReady + 2, bMmaDone = bOFinal + 2, kNumBars = bMmaDone + 2;
-static_assert(kOffP % 1024 == 0, "SWIZZLE_128B operands need 1024-byte alignment");
+              bQReady = bKvEmpty + NS_KV, bSFull = bQReady + 2, bPFull = bSFull + 4, bOReady = bPFull + 4,
+              bOFinal = bOReady + 2, bMmaDone = bOFinal + 2, kNumBars = bMmaDone + 2;  // S/P full: 2x + buffer
+static_assert(kOffQ % 1024 == 0, "SWIZZLE_128B operands need 1024-byte alignment");
 constexpr int kOffMisc = kOffBar + kNumBars * 8;
 constexpr int kSmemBytes = kOffMisc + 64 + 1024;  // + alignment slack
 
@@ -235,8 +236,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
     }
     for (int x = 0; x < 2; ++x) {
       mbar_init(&bars[bQReady + x], 4);
-      mbar_init(&bars[bSFull + x], 1);
-      mbar_init(&bars[bSFree + x], 4);
+      mbar_init(&bars[bSFull + 2 * x], 1);
+      mbar_init(&bars[bSFull + 2 * x + 1], 1);
       mbar_init(&bars[bPFull + 2 * x], 4);
       mbar_init(&bars[bPFull + 2 * x + 1], 4);
       mbar_init(&bars[bOReady + x], 1);
@@ -269,9 +270,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
     const int x = warp >> 2;
     const int r = tid - x * BM;
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    const uint32_t tQ = tmem + lane_off + kColQ + 64 * x;
     const uint32_t tO = tmem + lane_off + kColO + 128 * x;
-    const uint32_t tS = tmem + lane_off + kColS + 64 * x;
+    const uint32_t tS0 = tmem + lane_off + kColS + 128 * x;
     const int qi = q0 + x * BM + r;
     {
       uint32_t qw[64];
@@ -290,17 +290,21 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
 #pragma unroll
         for (int c = 0; c < 64; ++c) qw[c] = 0u;
       }
-      tmem_st32(tQ, reinterpret_cast<const uint32_t(&)[32]>(qw[0]));
-      tmem_st32(tQ + 32, reinterpret_cast<const uint32_t(&)[32]>(qw[32]));
-      tmem_wait_st();
-      tc_fence_before();
+      // row r of Q_x in the K-major SWIZZLE_128B layout of the S MMA's A operand
+      const uint32_t qdst = sbase + kOffQ + x * kQTile + r * 128;
+#pragma unroll
+      for (int c = 0; c < 16; ++c)
+        st_shared_v4(qdst + (c >> 3) * kQAtom + (((c & 7) ^ (r & 7)) << 4),
+                     make_uint4(qw[4 * c], qw[4 * c + 1], qw[4 * c + 2], qw[4 * c + 3]));
+      fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[bQReady + x]);
     }
     float m = -INFINITY, l = 0.0f;
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
-      if (!mbar_wait_warp(&bars[bSFull + x], j & 1, abort, &g_attn_status)) {
+      const uint32_t tS = tS0 + 64 * (j & 1);
+      if (!mbar_wait_warp(&bars[bSFull + 2 * x + (j & 1)], (j >> 1) & 1, abort, &g_attn_status)) {
         ok = false;
         break;
       }
@@ -309,10 +313,6 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
       tc_fence_after();
       uint32_t s0[32], s1[32];
       tmem_ld32x2_wait(tS, tS + 32, s0, s1);
-      // S_x(j) is in registers: the MMA may overwrite the buffer with S_x(j+1)
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars[bSFree + x]);
       const int valid = min(BN, a.Lk - j * BN);
       float mx = -INFINITY;
       if (valid == BN) {
@@ -338,12 +338,12 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
       }
       if (__any_sync(0xffffffffu, rescale)) {
         // O_x must hold every product up to PV_x(j-1) before it is rescaled:
-        // wait for S_x(j+1), issued behind PV_x(j-1) (S_x(j+2) needs this
-        // tile's next S-free, so the phase seen next step is still j+1), or,
+        // wait for S_x(j+1), issued behind PV_x(j-1) (the next commit into that
+        // buffer, S_x(j+3), follows PV_x(j+1), so the phase is unambiguous), or,
         // at the last tile, for the commit that follows PV_x(j-1).
         const bool last = j + 1 == nkv;
-        if (!mbar_wait_warp(&bars[last ? bOReady + x : bSFull + x], last ? 0u : static_cast<uint32_t>((j + 1) & 1),
-                            abort, &g_attn_status)) {
+        if (!mbar_wait_warp(&bars[last ? bOReady + x : bSFull + 2 * x + ((j + 1) & 1)],
+                            last ? 0u : static_cast<uint32_t>(((j + 1) >> 1) & 1), abort, &g_attn_status)) {
           ok = false;
           break;
         }
@@ -378,14 +378,9 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
         pw[16 + c] = pack_bf16x2(p2, p3);
       }
       l += sum;
-      // P_x(j) -> buffer j & 1, row r, K-major SWIZZLE_128B. The buffer was last
-      // read by PV_x(j-2), which completed before S_x(j) (issued behind it).
-      const uint32_t pdst = sbase + kOffP + (2 * x + (j & 1)) * kPTile + r * 128;
-#pragma unroll
-      for (int c = 0; c < 8; ++c)
-        st_shared_v4(pdst + ((c ^ (r & 7)) << 4), make_uint4(pw[4 * c], pw[4 * c + 1], pw[4 * c + 2], pw[4 * c + 3]));
-      fence_proxy_async_smem();
-      tc_fence_before();  // orders a rescale's TMEM stores before PV_x(j)
+      tmem_st32(tS, pw);  // P_x(j), 64 bf16 = 32 columns, over S_x(j)
+      tmem_wait_st();
+      tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[bPFull + 2 * x + (j & 1)]);
     }
@@ -491,23 +486,25 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
     if (lane == 0) {
       constexpr uint32_t idS = idesc_bf16(BM, BN, 0);
       constexpr uint32_t idPV = idesc_bf16(BM, D, 1);
-      const uint32_t tS = tmem + kColS + 64 * x, tQ = tmem + kColQ + 64 * x, tO = tmem + kColO + 128 * x;
+      const uint32_t tS0 = tmem + kColS + 128 * x, tO = tmem + kColO + 128 * x;
+      const uint32_t qaddr = sbase + kOffQ + x * kQTile;
+      // S_x(j) into buffer j & 1; Q and K K-major SWIZZLE_128B in shared memory
       auto issue_s = [&](int j) {
         const uint32_t kaddr = sbase + kOffK + (j % NS_KV) * kKVTile;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          mma_bf16_ts(tS, tQ + 8 * kk, smem_desc_sw128(kaddr + (kk >> 2) * kAtom + (kk & 3) * 32, 16, 1024), idS,
-                      kk > 0);
-        mma_commit(&bars[bSFull + x]);
+          mma_bf16_ss(tS0 + 64 * (j & 1), smem_desc_sw128(qaddr + (kk >> 2) * kQAtom + (kk & 3) * 32, 16, 1024),
+                      smem_desc_sw128(kaddr + (kk >> 2) * kAtom + (kk & 3) * 32, 16, 1024), idS, kk > 0);
+        mma_commit(&bars[bSFull + 2 * x + (j & 1)]);
       };
-      // O_x += P_x(j) V(j): P K-major from buffer j & 1, V MN-major
+      // O_x += P_x(j) V(j): P in TMEM over S_x(j), V MN-major
       auto issue_pv = [&](int j) {
         const uint32_t vaddr = sbase + kOffV + (j % NS_KV) * kKVTile;
-        const uint32_t paddr = sbase + kOffP + (2 * x + (j & 1)) * kPTile;
+        const uint32_t p = tS0 + 64 * (j & 1);
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk)
-          mma_bf16_ss(tO, smem_desc_sw128(paddr + kk * 32, 16, 1024), smem_desc_sw128(vaddr + kk * 2048, kAtom, 1024),
-                      idPV, (j > 0 || kk > 0) ? 1u : 0u);
+          mma_bf16_ts(tO, p + 8 * kk, smem_desc_sw128(vaddr + kk * 2048, kAtom, 1024), idPV,
+                      (j > 0 || kk > 0) ? 1u : 0u);
       };
       auto wait_kv = [&](int j) {
         return mbar_wait(&bars[bKvFull + j % NS_KV], (j / NS_KV) & 1, abort, &g_attn_status);
@@ -516,18 +513,23 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
       if (ok) {
         tc_fence_after();
         issue_s(0);
+        if (nkv > 1 && (ok = wait_kv(1))) {
+          tc_fence_after();
+          issue_s(1);
+        }
       }
       for (int j = 0; j < nkv && ok; ++j) {
-        if (j + 1 < nkv) {
-          // S_x(j+1) as soon as the softmax has taken S_x(j) out of TMEM
-          if (!(ok = wait_kv(j + 1) && mbar_wait(&bars[bSFree + x], j & 1, abort, &g_attn_status))) break;
-          tc_fence_after();
-          issue_s(j + 1);
-        }
         if (!(ok = mbar_wait(&bars[bPFull + 2 * x + (j & 1)], (j >> 1) & 1, abort, &g_attn_status))) break;
         tc_fence_after();
         issue_pv(j);
-        if (j + 2 == nkv) mma_commit(&bars[bOReady + x]);  // PV_x(nkv-2): a rescale at the last tile waits for it
+        if (j + 2 < nkv) {
+          // S_x(j+2) into the buffer PV_x(j) is reading: behind it in issue order
+          if (!(ok = wait_kv(j + 2))) break;
+          tc_fence_after();
+          issue_s(j + 2);
+        } else if (j + 2 == nkv) {
+          mma_commit(&bars[bOReady + x]);  // PV_x(nkv-2): a rescale at the last tile waits for it
+        }
       }
       if (ok) mma_commit(&bars[bOFinal + x]);
       // all MMAs issued by this thread have completed before TMEM is released
