@@ -238,13 +238,15 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
-def workload_config(world):
+def workload_config(world, gather="fused"):
     return {"workload": "int4-KV attention, window 3 frames (4680 tokens, 1560-token bf16 sink), "
                         "Q 4680 tokens, non-causal; bands4 groups",
             "streams": world, "heads": H_TOTAL, "heads_per_gpu": H_TOTAL // world, "lq": LQ, "lk": LK,
             "sink": SINK, "head_dim": D, "group_mode": MODE,
             "l2": f"{N_SETS} rotating input sets (Q + packed K/V + sink + out, ~{N_SETS * 160} MB) > 126 MB L2",
-            "parallelism": "single GPU" if world == 1 else f"head-sharded x{world} + NCCL all-gather"}
+            "parallelism": "single GPU" if world == 1 else (
+                f"head-sharded x{world}; output all-gather fused into the attention epilogue (NVLink peer stores)"
+                if gather == "fused" else f"head-sharded x{world} + NCCL all-gather")}
 
 
 # ----------------------------------------------------------------------------- our path
@@ -268,12 +270,16 @@ def run_ours(args):
     peaks = load_peaks()
 
     # ---- inputs resident in HBM: N_SETS rotating sets
-    sets = []
+    fused = world > 1 and args.gather == "fused"
+    sets, peers = [], []
     for i in range(N_SETS):
         tk, tv, _, _ = make_caches(B, LK, Hl, SINK, dev, seed=1000 * i, h0=h0)
         q = synth.make_q(B, LQ, Hl, seed=1000 * i + 7, device=dev)
         out = torch.empty_like(q)
         sets.append((q, tk, tv, out))
+        if fused:
+            # full-width output of the set on every rank, mapped into every peer
+            peers.append(shard.PeerOutputs(torch.empty((B, LQ, H_TOTAL, D), dtype=torch.bfloat16, device=dev)))
     gbuf = shard.gather_buffer(sets[0][3], world) if world > 1 else None
     torch.cuda.synchronize()
 
@@ -281,10 +287,13 @@ def run_ours(args):
         q, tk, tv, out = sets[i % N_SETS]
         if kev is not None:
             kev[0].record()
-        ops.attention_packed(q, tk, tv, 0, LK, out=out)
+        if fused:
+            ops.attention_packed_gather(q, tk, tv, 0, LK, peers[i % N_SETS].ptrs, h0, H_TOTAL)
+        else:
+            ops.attention_packed(q, tk, tv, 0, LK, out=out)
         if kev is not None:
             kev[1].record()
-        if world > 1:
+        if world > 1 and not fused:
             shard.gather_outputs(out, gbuf)
 
     for i in range(args.warmup):
@@ -333,7 +342,7 @@ def run_ours(args):
     line = {
         "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": t_ms / args.steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": DATA, "config": workload_config(world),
+        "vs_baseline": None, "dtype": "bf16", "data": DATA, "config": workload_config(world, args.gather),
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                      "frac": achieved / peaks["bf16_tflops"],
                      "traffic": traffic,
@@ -349,6 +358,9 @@ def run_ours(args):
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
+        dist.barrier()          # every rank is done storing into the peers' buffers
+        for p in peers:
+            p.close()
         dist.barrier()
         dist.destroy_process_group()
 
@@ -564,6 +576,8 @@ def main():
     ap.add_argument("--no-extras", action="store_true", help="skip quantize / prefill extras")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--gather", default="fused", choices=("fused", "nccl"),
+                    help="N > 1: all-gather of the output in the attention epilogue, or by NCCL")
     ap.add_argument("--profile-case", choices=("attention", "quantize", "dequantize"),
                     help="run a few launches of one kernel for an ncu capture and exit")
     args = ap.parse_args()

@@ -45,7 +45,10 @@ extern "C" {
 #define KVQ_ERR_DEVICE (-5)      /* the current device is not an sm_100 part */
 
 /* ABI version of this header; bumped on any signature change. */
-#define KVQ_ABI_VERSION 1
+#define KVQ_ABI_VERSION 2
+
+/* Size of the opaque handle kvq_ipc_export() writes (a cudaIpcMemHandle_t). */
+#define KVQ_IPC_HANDLE_BYTES 64
 
 KVQ_API int kvq_abi_version(void);
 
@@ -114,6 +117,40 @@ KVQ_API int kvq_attention(const void* q, int64_t q_token_stride,
                           void* out, int64_t out_token_stride, int batch, int64_t n_q,
                           int n_heads, int head_dim, const int32_t* chan_band, int n_groups,
                           int k_bits, int v_bits, float softmax_scale, void* stream);
+
+/*
+ * kvq_attention() for one rank of a head-sharded job: the n_heads heads of this
+ * launch are written at heads [out_head0, out_head0 + n_heads) of each of the
+ * n_outs output buffers outs[0..n_outs) (1 <= n_outs <= 8), all of layout
+ * [batch, n_q, out_heads, head_dim] bf16 with token stride out_token_stride
+ * (elements, >= out_heads * head_dim, multiple of 8; buffers 16-byte aligned).
+ * With outs = every rank's output buffer (peers mapped by kvq_ipc_import()),
+ * the epilogue is the all-gather of the output over NVLink: when every rank's
+ * launch has completed, every rank holds the full [batch, n_q, out_heads, D].
+ * Other arguments and errors as kvq_attention(). No counterpart in the
+ * reference (single GPU); replaces the attention + NCCL all-gather pair of a
+ * head-sharded deployment.
+ */
+KVQ_API int kvq_attention_gather(const void* q, int64_t q_token_stride,
+                                 const void* k_codes, const void* k_scales, const void* k_sink,
+                                 const void* v_codes, const void* v_scales, const void* v_sink,
+                                 int64_t cache_tokens, int64_t sink_tokens, int64_t lo, int64_t hi,
+                                 void* const* outs, int n_outs, int out_head0, int out_heads,
+                                 int64_t out_token_stride, int batch, int64_t n_q,
+                                 int n_heads, int head_dim, const int32_t* chan_band, int n_groups,
+                                 int k_bits, int v_bits, float softmax_scale, void* stream);
+
+/*
+ * CUDA IPC for the output buffers of kvq_attention_gather(). kvq_ipc_export()
+ * writes KVQ_IPC_HANDLE_BYTES bytes naming the device allocation that contains
+ * ptr and the byte offset of ptr in it; another process passes both to
+ * kvq_ipc_import(), which maps the allocation (*base) and returns the address of
+ * ptr there (*ptr); kvq_ipc_close(base) unmaps it. No counterpart in the
+ * reference (single GPU).
+ */
+KVQ_API int kvq_ipc_export(const void* ptr, void* handle, int64_t* offset);
+KVQ_API int kvq_ipc_import(const void* handle, int64_t offset, void** base, void** ptr);
+KVQ_API int kvq_ipc_close(void* base);
 
 /*
  * Synchronizes the current device and returns the library's device status word:

@@ -89,6 +89,8 @@ static_assert(kOffQ % 1024 == 0, "SWIZZLE_128B operands need 1024-byte alignment
 constexpr int kOffMisc = kOffBar + kNumBars * 8;
 constexpr int kSmemBytes = kOffMisc + 64 + 1024;  // + alignment slack
 
+constexpr int kMaxOut = 8;
+
 struct alignas(64) Args {
   CUtensorMap tm_kc, tm_vc;  // codes [B*S rows, H*64 B], box 64 x 64, SWIZZLE_64B
   CUtensorMap tm_ks, tm_vs;  // sinks [B*sink rows, H*128 bf16], box 64 x 64, SWIZZLE_128B
@@ -98,7 +100,8 @@ struct alignas(64) Args {
   const uint16_t* vs;
   int64_t cache_tokens, sink_tokens, lo;
   int Lk, Lq, H;
-  uint16_t* out;
+  uint16_t* out[kMaxOut];  // n_out destinations of identical layout (this GPU's and peers')
+  int n_out, out_head0;     // heads of this launch land at heads out_head0.. of each destination
   int64_t o_tok_stride, o_batch_stride;
   float scale_log2;
 };
@@ -387,22 +390,31 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
     if (ok && mbar_wait_warp(&bars[bOFinal + x], 0, abort, &g_attn_status)) {
       tc_fence_after();
       const float inv = 1.0f / l;
-      uint16_t* dst = a.out + b * a.o_batch_stride + static_cast<int64_t>(qi) * a.o_tok_stride +
-                      static_cast<int64_t>(h) * D;
+      const int64_t off = b * a.o_batch_stride + static_cast<int64_t>(qi) * a.o_tok_stride +
+                          static_cast<int64_t>(a.out_head0 + h) * D;
 #pragma unroll 1
       for (int k = 0; k < 4; ++k) {
         uint32_t o[32];
         tmem_ld32_wait(tO + 32 * k, o);
         if (qi < a.Lq) {
+          uint4 v[4];
 #pragma unroll
           for (int c = 0; c < 4; ++c)
-            st_global_v4(dst + 32 * k + 8 * c,
-                         make_uint4(pack_bf16x2(__uint_as_float(o[8 * c + 0]) * inv, __uint_as_float(o[8 * c + 1]) * inv),
-                                    pack_bf16x2(__uint_as_float(o[8 * c + 2]) * inv, __uint_as_float(o[8 * c + 3]) * inv),
-                                    pack_bf16x2(__uint_as_float(o[8 * c + 4]) * inv, __uint_as_float(o[8 * c + 5]) * inv),
-                                    pack_bf16x2(__uint_as_float(o[8 * c + 6]) * inv, __uint_as_float(o[8 * c + 7]) * inv)));
+            v[c] = make_uint4(pack_bf16x2(__uint_as_float(o[8 * c + 0]) * inv, __uint_as_float(o[8 * c + 1]) * inv),
+                              pack_bf16x2(__uint_as_float(o[8 * c + 2]) * inv, __uint_as_float(o[8 * c + 3]) * inv),
+                              pack_bf16x2(__uint_as_float(o[8 * c + 4]) * inv, __uint_as_float(o[8 * c + 5]) * inv),
+                              pack_bf16x2(__uint_as_float(o[8 * c + 6]) * inv, __uint_as_float(o[8 * c + 7]) * inv));
+          // the row goes to every destination: with peer buffers (mapped over
+          // NVLink) this epilogue is the all-gather of the head-sharded output
+#pragma unroll 1
+          for (int d = 0; d < a.n_out; ++d)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) st_global_v4(a.out[d] + off + 32 * k + 8 * c, v[c]);
         }
       }
+      // No fence: the peer stores drain while the SM runs its next CTA; the
+      // consumer orders them by the kernel's completion (stream synchronize on
+      // the writing rank, then a cross-rank barrier).
     }
   } else if (warp < kProdWarp) {
     // ------------------------------------------------------------ converters
@@ -605,13 +617,12 @@ int launch(const Args& a, int n_ctas, int batch, cudaStream_t st) {
 
 using namespace kvq;
 
-extern "C" int kvq_attention(const void* q, int64_t q_token_stride, const void* k_codes, const void* k_scales,
-                             const void* k_sink, const void* v_codes, const void* v_scales, const void* v_sink,
-                             int64_t cache_tokens, int64_t sink_tokens, int64_t lo, int64_t hi, void* out,
-                             int64_t out_token_stride, int batch, int64_t n_q, int n_heads, int head_dim,
-                             const int32_t* chan_band, int n_groups, int k_bits, int v_bits, float softmax_scale,
-                             void* stream) {
-  clear_error();
+static int attention_impl(const void* q, int64_t q_token_stride, const void* k_codes, const void* k_scales,
+                          const void* k_sink, const void* v_codes, const void* v_scales, const void* v_sink,
+                          int64_t cache_tokens, int64_t sink_tokens, int64_t lo, int64_t hi, void* const* outs,
+                          int n_outs, int out_head0, int out_heads, int64_t out_token_stride, int batch, int64_t n_q,
+                          int n_heads, int head_dim, const int32_t* chan_band, int n_groups, int k_bits, int v_bits,
+                          float softmax_scale, void* stream) {
   KVQ_REQUIRE(head_dim == 128, KVQ_ERR_UNSUPPORTED, "attention supports head_dim 128, got %d", head_dim);
   KVQ_REQUIRE(k_bits == 4 && v_bits == 4, KVQ_ERR_UNSUPPORTED, "attention reads int4 K and V (got %d/%d bits)",
               k_bits, v_bits);
@@ -631,12 +642,18 @@ extern "C" int kvq_attention(const void* q, int64_t q_token_stride, const void* 
   KVQ_REQUIRE(layout != kLayoutGeneric, KVQ_ERR_UNSUPPORTED,
               "attention supports the bands, bands2, bands4, blind32 and blind64 group maps");
   if (n_q == 0) return KVQ_OK;
-  KVQ_REQUIRE(q && k_codes && k_scales && v_codes && v_scales && out, KVQ_ERR_ARG, "NULL data pointer");
-  KVQ_REQUIRE(q_token_stride >= (int64_t)n_heads * head_dim && out_token_stride >= (int64_t)n_heads * head_dim,
-              KVQ_ERR_ARG, "token strides must be >= n_heads*head_dim");
+  KVQ_REQUIRE(outs && n_outs >= 1 && n_outs <= attn::kMaxOut, KVQ_ERR_ARG, "1 to %d outputs, got %d",
+              attn::kMaxOut, n_outs);
+  KVQ_REQUIRE(out_head0 >= 0 && out_head0 + n_heads <= out_heads, KVQ_ERR_ARG,
+              "heads [%d, %d) do not fit an output of %d heads", out_head0, out_head0 + n_heads, out_heads);
+  KVQ_REQUIRE(q && k_codes && k_scales && v_codes && v_scales, KVQ_ERR_ARG, "NULL data pointer");
+  for (int d = 0; d < n_outs; ++d) KVQ_REQUIRE(outs[d], KVQ_ERR_ARG, "NULL output pointer %d", d);
+  KVQ_REQUIRE(q_token_stride >= (int64_t)n_heads * head_dim && out_token_stride >= (int64_t)out_heads * head_dim,
+              KVQ_ERR_ARG, "token strides must be >= heads*head_dim");
   auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
-  KVQ_REQUIRE(al16(q) && al16(out) && q_token_stride % 8 == 0 && out_token_stride % 8 == 0, KVQ_ERR_ALIGN,
+  KVQ_REQUIRE(al16(q) && q_token_stride % 8 == 0 && out_token_stride % 8 == 0, KVQ_ERR_ALIGN,
               "q and out must be 16-byte aligned with token strides that are multiples of 8");
+  for (int d = 0; d < n_outs; ++d) KVQ_REQUIRE(al16(outs[d]), KVQ_ERR_ALIGN, "output %d is not 16-byte aligned", d);
   KVQ_REQUIRE(al16(k_codes) && al16(v_codes) && (!k_sink || al16(k_sink)) && (!v_sink || al16(v_sink)),
               KVQ_ERR_ALIGN, "codes and sink buffers must be 16-byte aligned");
   const int sa = (n_groups * 2) % 8 == 0 ? 8 : (n_groups * 2) % 4 == 0 ? 4 : 2;
@@ -674,7 +691,9 @@ extern "C" int kvq_attention(const void* q, int64_t q_token_stride, const void* 
   a.Lk = static_cast<int>(hi - lo);
   a.Lq = static_cast<int>(n_q);
   a.H = n_heads;
-  a.out = static_cast<uint16_t*>(out);
+  for (int d = 0; d < n_outs; ++d) a.out[d] = static_cast<uint16_t*>(outs[d]);
+  a.n_out = n_outs;
+  a.out_head0 = out_head0;
   a.o_tok_stride = out_token_stride;
   a.o_batch_stride = out_token_stride * n_q;
   const float sc = softmax_scale > 0.0f ? softmax_scale : 1.0f / sqrtf(static_cast<float>(head_dim));
@@ -691,6 +710,36 @@ extern "C" int kvq_attention(const void* q, int64_t q_token_stride, const void* 
   }
   set_error("internal: unhandled layout %d", layout);
   return KVQ_ERR_UNSUPPORTED;
+}
+
+extern "C" int kvq_attention(const void* q, int64_t q_token_stride, const void* k_codes, const void* k_scales,
+                             const void* k_sink, const void* v_codes, const void* v_scales, const void* v_sink,
+                             int64_t cache_tokens, int64_t sink_tokens, int64_t lo, int64_t hi, void* out,
+                             int64_t out_token_stride, int batch, int64_t n_q, int n_heads, int head_dim,
+                             const int32_t* chan_band, int n_groups, int k_bits, int v_bits, float softmax_scale,
+                             void* stream) {
+  clear_error();
+  void* outs[1] = {out};
+  if (n_q > 0 && !out) {
+    set_error("NULL data pointer");
+    return KVQ_ERR_ARG;
+  }
+  return attention_impl(q, q_token_stride, k_codes, k_scales, k_sink, v_codes, v_scales, v_sink, cache_tokens,
+                        sink_tokens, lo, hi, outs, 1, 0, n_heads, out_token_stride, batch, n_q, n_heads, head_dim,
+                        chan_band, n_groups, k_bits, v_bits, softmax_scale, stream);
+}
+
+extern "C" int kvq_attention_gather(const void* q, int64_t q_token_stride, const void* k_codes,
+                                    const void* k_scales, const void* k_sink, const void* v_codes,
+                                    const void* v_scales, const void* v_sink, int64_t cache_tokens,
+                                    int64_t sink_tokens, int64_t lo, int64_t hi, void* const* outs, int n_outs,
+                                    int out_head0, int out_heads, int64_t out_token_stride, int batch, int64_t n_q,
+                                    int n_heads, int head_dim, const int32_t* chan_band, int n_groups, int k_bits,
+                                    int v_bits, float softmax_scale, void* stream) {
+  clear_error();
+  return attention_impl(q, q_token_stride, k_codes, k_scales, k_sink, v_codes, v_scales, v_sink, cache_tokens,
+                        sink_tokens, lo, hi, outs, n_outs, out_head0, out_heads, out_token_stride, batch, n_q,
+                        n_heads, head_dim, chan_band, n_groups, k_bits, v_bits, softmax_scale, stream);
 }
 
 extern "C" int kvq_device_status(int reset) {

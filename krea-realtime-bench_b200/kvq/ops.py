@@ -151,6 +151,67 @@ def attention_packed(q: torch.Tensor, k_cache, v_cache, lo: int, hi: int, out: t
     return out
 
 
+def attention_packed_gather(q: torch.Tensor, k_cache, v_cache, lo: int, hi: int, outs: list[int],
+                            out_head0: int, out_heads: int, out_token_stride: int | None = None,
+                            softmax_scale: float | None = None) -> None:
+    """Head-sharded attention whose epilogue is the output all-gather: the H heads
+    of q [B, Lq, H, D] (heads out_head0.. of the full model) are written into each
+    of the device buffers `outs` (raw pointers, e.g. PeerOutputs.ptrs: this GPU's
+    and its peers'), all laid out [B, Lq, out_heads, D] bf16 with the given token
+    stride (default out_heads * D)."""
+    dev = _require_cuda(q, k_cache.packed, v_cache.packed)
+    if q.dtype != torch.bfloat16 or q.dim() != 4:
+        raise TypeError("q must be a [B, Lq, H, D] bfloat16 tensor")
+    B, Lq, H, D = q.shape
+    for c in (k_cache, v_cache):
+        if (c.n_streams, c.n_heads, c.head_dim) != (B, H, D):
+            raise ValueError(f"cache shape {tuple(c.shape)} does not match q {tuple(q.shape)}")
+    if (k_cache.n_tokens, k_cache.sink_tokens, k_cache.bands) != (v_cache.n_tokens, v_cache.sink_tokens,
+                                                                  v_cache.bands):
+        raise ValueError("K and V caches must share tokens, sink and group mode")
+    if not 1 <= len(outs) <= 8:
+        raise ValueError(f"1 to 8 output buffers, got {len(outs)}")
+    if q.stride(3) != 1 or q.stride(2) != D or q.stride(0) != Lq * q.stride(1):
+        q = q.contiguous()
+    stride = out_heads * D if out_token_stride is None else int(out_token_stride)
+    arr = (ctypes.c_void_p * len(outs))(*[ctypes.c_void_p(int(p)) for p in outs])
+    cb = _host_map(k_cache.chan_band_host)
+    with torch.cuda.device(dev):
+        rc = _lib.load().kvq_attention_gather(
+            _ptr(q), q.stride(1), _ptr(k_cache.packed), _ptr(k_cache.scales), _ptr(k_cache.sink),
+            _ptr(v_cache.packed), _ptr(v_cache.scales), _ptr(v_cache.sink), k_cache.n_tokens,
+            k_cache.sink_tokens if k_cache.sink is not None else 0, int(lo), int(hi),
+            ctypes.cast(arr, ctypes.c_void_p), len(outs), int(out_head0), int(out_heads), stride,
+            B, Lq, H, D, cb.ctypes.data_as(ctypes.c_void_p), len(k_cache.bands), k_cache.bits, v_cache.bits,
+            float(softmax_scale) if softmax_scale else 0.0, _stream(dev))
+    _lib.check(rc, "kvq_attention_gather")
+
+
+def ipc_export(t: torch.Tensor) -> tuple[bytes, int]:
+    """(handle, byte offset) naming the CUDA allocation that holds t, for
+    ipc_import() in another process."""
+    _require_cuda(t)
+    h = ctypes.create_string_buffer(_lib.IPC_HANDLE_BYTES)
+    off = ctypes.c_int64()
+    with torch.cuda.device(t.device):
+        _lib.check(_lib.load().kvq_ipc_export(_ptr(t), h, ctypes.byref(off)), "kvq_ipc_export")
+    return h.raw, off.value
+
+
+def ipc_import(handle: bytes, offset: int) -> tuple[int, int]:
+    """Maps another process's allocation on the current device; returns (base, ptr)."""
+    if len(handle) != _lib.IPC_HANDLE_BYTES:
+        raise ValueError("bad IPC handle")
+    base, ptr = ctypes.c_void_p(), ctypes.c_void_p()
+    _lib.check(_lib.load().kvq_ipc_import(handle, int(offset), ctypes.byref(base), ctypes.byref(ptr)),
+               "kvq_ipc_import")
+    return base.value, ptr.value
+
+
+def ipc_close(base: int) -> None:
+    _lib.check(_lib.load().kvq_ipc_close(ctypes.c_void_p(base)), "kvq_ipc_close")
+
+
 def device_status(reset: bool = True) -> int:
     """Synchronizes and returns the library's device status word (0 = ok)."""
     rc = _lib.load().kvq_device_status(1 if reset else 0)

@@ -2,9 +2,11 @@
 
 The 40 heads are split in contiguous ranges over the ranks (40/20/10/5 per GPU
 on 1/2/4/8 B200s); each rank holds the cache of its heads only and runs the
-attention for them on all streams; one NCCL all-gather over NVLink collects the
-attention outputs. The reference is single-GPU throughout, so this module has no
-counterpart there.
+attention for them on all streams. The outputs are all-gathered either by the
+attention kernel itself (PeerOutputs: every rank's full-width output buffer is
+mapped into every other rank, and the epilogue stores each output row into all
+of them over NVLink) or by one NCCL all-gather (gather_outputs). The reference
+is single-GPU throughout, so this module has no counterpart there.
 """
 from __future__ import annotations
 
@@ -47,3 +49,52 @@ def assemble_heads(gathered: torch.Tensor) -> torch.Tensor:
     """[world, B, Lq, Hl, D] -> [B, Lq, world*Hl, D] in global head order."""
     w, B, Lq, Hl, D = gathered.shape
     return gathered.permute(1, 2, 0, 3, 4).reshape(B, Lq, w * Hl, D)
+
+
+class PeerOutputs:
+    """A full-width output buffer [B, Lq, H, D] bf16 on every rank, mapped into
+    every other rank (CUDA IPC), for ops.attention_packed_gather(). `ptrs` lists
+    the buffers rank by rank, this rank's own first-hand pointer included; after
+    every rank's gather launch of a step has completed (e.g. a barrier after the
+    synchronize), `local` holds the whole step's output on every rank.
+
+    `exchange` is the collective that gathers one picklable object per rank
+    (dist.all_gather_object by default); `ops` provides ipc_export / ipc_import /
+    ipc_close (both replaceable for tests without GPUs)."""
+
+    def __init__(self, local: torch.Tensor, group=None, exchange=None, ops=None):
+        if ops is None:
+            from . import ops as _ops
+            ops = _ops
+        self._ops = ops
+        self.local = local
+        world = dist.get_world_size(group)
+        rank = dist.get_rank(group)
+        if exchange is None:
+            def exchange(obj):
+                got = [None] * world
+                dist.all_gather_object(got, obj, group=group)
+                return got
+        mine = ops.ipc_export(local)
+        got = exchange(mine)
+        if len(got) != world:
+            raise RuntimeError(f"exchange returned {len(got)} entries for {world} ranks")
+        self.ptrs: list[int] = []
+        self._bases: list[int] = []
+        try:
+            for r, (handle, offset) in enumerate(got):
+                if r == rank:
+                    self.ptrs.append(local.data_ptr())
+                else:
+                    base, ptr = ops.ipc_import(handle, offset)
+                    self._bases.append(base)
+                    self.ptrs.append(ptr)
+        except Exception:
+            self.close()
+            raise
+
+    def close(self) -> None:
+        """Unmaps the peers' buffers (call before the peers free theirs)."""
+        bases, self._bases = self._bases, []
+        for b in bases:
+            self._ops.ipc_close(b)

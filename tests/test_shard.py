@@ -91,3 +91,52 @@ def test_dead_rank_is_an_error_not_a_hang():
     import sys
     codes = _run(_failing_worker, 2, [p for p in sys.path if p])
     assert codes[1] == 7 and codes[0] == 11
+
+
+class _FakeIpc:
+    """Stands in for kvq.ops' CUDA IPC calls: a 'handle' names the exporting rank."""
+
+    def __init__(self, rank):
+        self.rank = rank
+        self.opened, self.closed = [], []
+
+    def ipc_export(self, t):
+        return (b"rank%d" % self.rank).ljust(64, b"\0"), 16 * self.rank
+
+    def ipc_import(self, handle, offset):
+        peer = int(handle.rstrip(b"\0")[4:])
+        assert offset == 16 * peer
+        base = 1000 * (peer + 1)
+        self.opened.append(base)
+        return base, base + offset
+
+    def ipc_close(self, base):
+        self.closed.append(base)
+
+
+def _peer_worker(rank, world, port, paths):
+    import datetime
+    import sys
+    sys.path[:0] = paths
+    import torch.distributed as dist
+    from kvq import shard
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
+    fake = _FakeIpc(rank)
+    local = torch.zeros(4)
+    po = shard.PeerOutputs(local, ops=fake)
+    want = [local.data_ptr() if r == rank else 1000 * (r + 1) + 16 * r for r in range(world)]
+    ok = po.ptrs == want and len(fake.opened) == world - 1
+    po.close()
+    po.close()  # idempotent
+    ok = ok and sorted(fake.closed) == sorted(fake.opened)
+    dist.destroy_process_group()
+    if not ok:
+        raise SystemExit(3)
+
+
+def test_peer_outputs_exchange_three_ranks():
+    """Every rank ends with the buffers of all ranks in rank order: its own
+    pointer first-hand, the peers' through their exported handles and offsets."""
+    import sys
+    assert _run(_peer_worker, 3, [p for p in sys.path if p]) == [0, 0, 0]
