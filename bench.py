@@ -490,6 +490,24 @@ def run_extras(dev, peaks):
         del xs, cs, ss, outs
         torch.cuda.empty_cache()
 
+    # the append of one block to all 40 layers x {K, V} in one launch (kvq_rebuild_layers)
+    nt = 80
+    xs = [synth.make_k(LK, H_TOTAL, seed=700 + (i % 8), device=dev) for i in range(8)]
+    cs = [torch.empty((LK, H_TOTAL, D // 2), dtype=torch.uint8, device=dev) for _ in range(nt)]
+    ss = [torch.empty((LK, H_TOTAL, G), dtype=torch.bfloat16, device=dev) for _ in range(nt)]
+    xin = [xs[i % 8] for i in range(nt)]
+
+    def fb(_i):
+        ops.quantize_layers_into(xin, cs, ss, cb, G, 4)
+    ms = _time_events(fb, 10)
+    byts = nt * LK * H_TOTAL * quant_bytes_per_row(G)
+    gbs = byts / (statistics.median(ms) / 1e3) / 1e9
+    res["quantize_append_40layers_kv_4680_one_launch"] = {
+        "gbs": gbs, "ms": statistics.median(ms), "bytes": byts, "frac_hbm": gbs / peaks["hbm_gbs"],
+        "note": "8 distinct inputs cycled over the 80 tensors (inputs 384 MB > L2)"}
+    del xs, cs, ss, xin
+    torch.cuda.empty_cache()
+
     # prefill (rebuild) per block, 40 layers: quantize the window's K and V into
     # the cache, then attention of the window's queries over the window; and the
     # 4 denoising steps' attention (4680 queries) over the same window

@@ -119,6 +119,22 @@ KVQ_API int kvq_attention(const void* q, int64_t q_token_stride,
                           int k_bits, int v_bits, float softmax_scale, void* stream);
 
 /*
+ * kvq_quantize() of the same token range of n_tensors tensors (1..96, e.g. the
+ * 40 layers x {K, V} of a window rebuild) in one launch: tensor i reads x[i]
+ * and writes codes[i], scales[i] and, for its first sink_tokens tokens,
+ * sink[i] (sink may be NULL for no sink copy; single entries may be NULL too).
+ * All tensors share n_tokens, n_heads, head_dim, x_token_stride, the group map
+ * and bits; every pointer has the alignment kvq_quantize() requires. Results are
+ * bit-identical to n_tensors kvq_quantize() calls. Replaces the per-layer
+ * quantize launches of a rebuild (quant_kv_kernels.py:102-111 called once per
+ * layer and tensor through quant_kv.py:212-215).
+ */
+KVQ_API int kvq_rebuild_layers(int n_tensors, const void* const* x, int64_t x_token_stride,
+                               void* const* codes, void* const* scales, void* const* sink,
+                               int64_t sink_tokens, int64_t n_tokens, int n_heads, int head_dim,
+                               const int32_t* chan_band, int n_groups, int bits, void* stream);
+
+/*
  * kvq_attention() for one rank of a head-sharded job: the n_heads heads of this
  * launch are written at heads [out_head0, out_head0 + n_heads) of each of the
  * n_outs output buffers outs[0..n_outs) (1 <= n_outs <= 8), all of layout

@@ -45,6 +45,23 @@ struct QuantArgs {
   int rows_contig;  // x_token_stride == H * D
 };
 
+// Up to kMaxTensors tensors of identical shape quantized by one launch (the
+// layers x {K, V} of a rebuild); tile t of the launch is tile t % tiles_per of
+// tensor t / tiles_per.
+constexpr int kMaxTensors = 96;
+struct QuantBatch {
+  QuantArgs t[kMaxTensors];
+  int n;
+  int64_t tiles_per;
+  __device__ __forceinline__ const QuantArgs& tensor(int64_t i) const { return t[i]; }
+};
+// One tensor: the small parameter block of a plain launch (no indexed lookups).
+struct QuantOne {
+  QuantArgs a;
+  int64_t tiles_per;
+  __device__ __forceinline__ const QuantArgs& tensor(int64_t) const { return a; }
+};
+
 __device__ __forceinline__ const uint16_t* x_row_ptr(const QuantArgs& a, int64_t row, int D) {
   if (a.rows_contig) return a.x + row * D;
   int64_t t = row / a.H;
@@ -227,8 +244,8 @@ constexpr int pipe_smem_bytes() {
 // Persistent CTAs walk the 128-row tiles with a grid stride; each thread keeps
 // the next kStages-1 tiles' input in flight (cp.async, 16 bytes per copy, into
 // the XOR-swizzled layout) while it quantizes its row of the current tile.
-template <class L, int BITS>
-__global__ void __launch_bounds__(kQT, 3) quantize_rows_pipe(QuantArgs a, int64_t n_tiles) {
+template <class L, int BITS, class P>
+__global__ void __launch_bounds__(kQT, 3) quantize_rows_pipe(const __grid_constant__ P bt, int64_t n_tiles) {
   using C = QuantConsts<BITS>;
   constexpr int G = L::G;
   constexpr int S = PipeCfg<BITS>::kStages;
@@ -241,8 +258,19 @@ __global__ void __launch_bounds__(kQT, 3) quantize_rows_pipe(QuantArgs a, int64_
   const int tid = threadIdx.x;
   const uint32_t in_base = static_cast<uint32_t>(__cvta_generic_to_shared(sm_in));
 
-  auto issue = [&](int64_t tile, int stage) {
-    const int64_t row0 = tile * kQT;
+  // A launch tile is (tensor ti, tile loc of it). The grid-stride walk advances
+  // (ti, loc) by additions; a division only places the first tiles.
+  const int64_t tpt = bt.tiles_per;
+  auto advance = [&](int64_t& ti, int64_t& loc) {
+    loc += gridDim.x;
+    while (loc >= tpt) {
+      loc -= tpt;
+      ++ti;
+    }
+  };
+  auto issue = [&](int64_t ti, int64_t loc, int stage) {
+    const QuantArgs& a = bt.tensor(ti);
+    const int64_t row0 = loc * kQT;
     const int nrows = static_cast<int>(min(static_cast<int64_t>(kQT), a.n_rows - row0));
 #pragma unroll 4
     for (int i = tid; i < kQT * 16; i += kQT) {
@@ -258,22 +286,28 @@ __global__ void __launch_bounds__(kQT, 3) quantize_rows_pipe(QuantArgs a, int64_
 #pragma unroll
   for (int s = 0; s < S - 1; ++s) {
     const int64_t t = first + static_cast<int64_t>(s) * gridDim.x;
-    if (t < n_tiles) issue(t, s);
+    if (t < n_tiles) issue(t / tpt, t % tpt, s);
     cp_async_commit();
   }
+  int64_t ci = first / tpt, cl = first % tpt;  // the tile processed next
+  const int64_t fn = first + static_cast<int64_t>(S - 1) * gridDim.x;
+  int64_t ni = fn / tpt, nl = fn % tpt;        // the tile prefetched next
   for (int64_t k = 0;; ++k) {
     const int64_t tile = first + k * gridDim.x;
     if (tile >= n_tiles) break;
     {
       const int64_t tn = tile + static_cast<int64_t>(S - 1) * gridDim.x;
-      if (tn < n_tiles) issue(tn, static_cast<int>((k + S - 1) % S));
+      if (tn < n_tiles) issue(ni, nl, static_cast<int>((k + S - 1) % S));
       cp_async_commit();
+      advance(ni, nl);
     }
     cp_async_wait<S - 1>();
     __syncthreads();
     const int stage = static_cast<int>(k % S);
     const uint4* tin = sm_in + stage * kQT * 16;
-    const int64_t row0 = tile * kQT;
+    const QuantArgs& a = bt.tensor(ci);
+    const int64_t row0 = cl * kQT;
+    advance(ci, cl);
     const int nrows = static_cast<int>(min(static_cast<int64_t>(kQT), a.n_rows - row0));
     if (tid < nrows) {
       uint32_t w[64];
@@ -605,8 +639,8 @@ static int num_sms() {
   return sms[dev];
 }
 
-template <class L, int BITS>
-static int launch_fast(const QuantArgs& a, cudaStream_t st) {
+template <class L, int BITS, class P>
+static int launch_fast(const P& b, int64_t tiles, cudaStream_t st) {
   constexpr int smem = pipe_smem_bytes<L, BITS>();
   constexpr int per_sm = (227 * 1024) / smem < 3 ? (227 * 1024) / smem : 3;  // 3 for int4, 2 for int8
   static_assert(per_sm >= 2, "at least two CTAs per SM must fit");
@@ -615,7 +649,7 @@ static int launch_fast(const QuantArgs& a, cudaStream_t st) {
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(quantize_rows_pipe<L, BITS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(quantize_rows_pipe<L, BITS, P>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          smem);
     if (e != cudaSuccess) {
       set_error("cudaFuncSetAttribute(quantize): %s", cudaGetErrorString(e));
@@ -623,21 +657,20 @@ static int launch_fast(const QuantArgs& a, cudaStream_t st) {
     }
     configured[dev] = true;
   }
-  const int64_t tiles = (a.n_rows + kQT - 1) / kQT;
   const int64_t cap = static_cast<int64_t>(per_sm) * num_sms();
   const unsigned grid = static_cast<unsigned>(tiles < cap ? tiles : cap);
-  quantize_rows_pipe<L, BITS><<<grid, kQT, smem, st>>>(a, tiles);
+  quantize_rows_pipe<L, BITS, P><<<grid, kQT, smem, st>>>(b, tiles);
   return check_launch("kvq_quantize");
 }
 
-template <int BITS>
-static int dispatch_fast(int layout, const QuantArgs& a, cudaStream_t st) {
+template <int BITS, class P>
+static int dispatch_fast(int layout, const P& a, int64_t tiles, cudaStream_t st) {
   switch (layout) {
-    case kLayoutBands: return launch_fast<LayoutBands, BITS>(a, st);
-    case kLayoutBands2: return launch_fast<LayoutBands2, BITS>(a, st);
-    case kLayoutBands4: return launch_fast<LayoutBands4, BITS>(a, st);
-    case kLayoutBlind32: return launch_fast<LayoutBlind32, BITS>(a, st);
-    case kLayoutBlind64: return launch_fast<LayoutBlind64, BITS>(a, st);
+    case kLayoutBands: return launch_fast<LayoutBands, BITS>(a, tiles, st);
+    case kLayoutBands2: return launch_fast<LayoutBands2, BITS>(a, tiles, st);
+    case kLayoutBands4: return launch_fast<LayoutBands4, BITS>(a, tiles, st);
+    case kLayoutBlind32: return launch_fast<LayoutBlind32, BITS>(a, tiles, st);
+    case kLayoutBlind64: return launch_fast<LayoutBlind64, BITS>(a, tiles, st);
     default: break;
   }
   set_error("internal: no specialised kernel for layout %d", layout);
@@ -668,6 +701,66 @@ static int launch_dequant(const DequantArgs& a, cudaStream_t st) {
 
 using namespace kvq;
 
+// Checks of one tensor's pointers for kvq_quantize / kvq_rebuild_layers.
+static int check_quant_tensor(const void* x, int64_t x_token_stride, const void* codes, const void* scales,
+                              const void* sink, int n_heads, int head_dim, int index) {
+  KVQ_REQUIRE(x && codes && scales, KVQ_ERR_ARG, "NULL data pointer (tensor %d)", index);
+  KVQ_REQUIRE(x_token_stride >= static_cast<int64_t>(n_heads) * head_dim, KVQ_ERR_ARG,
+              "x_token_stride %lld < n_heads*head_dim", (long long)x_token_stride);
+  KVQ_REQUIRE((reinterpret_cast<uintptr_t>(x) & 15) == 0 && (x_token_stride % 8) == 0, KVQ_ERR_ALIGN,
+              "x must be 16-byte aligned with a token stride that is a multiple of 8 elements (tensor %d)", index);
+  KVQ_REQUIRE((reinterpret_cast<uintptr_t>(codes) & 15) == 0, KVQ_ERR_ALIGN,
+              "codes must be 16-byte aligned (tensor %d)", index);
+  KVQ_REQUIRE((reinterpret_cast<uintptr_t>(scales) & 1) == 0, KVQ_ERR_ALIGN,
+              "scales must be 2-byte aligned (tensor %d)", index);
+  KVQ_REQUIRE(sink == nullptr || (reinterpret_cast<uintptr_t>(sink) & 15) == 0, KVQ_ERR_ALIGN,
+              "sink must be 16-byte aligned (tensor %d)", index);
+  return KVQ_OK;
+}
+
+static QuantArgs quant_args(const void* x, int64_t x_token_stride, void* codes, void* scales, void* sink,
+                            int64_t sink_tokens, int64_t n_tokens, int n_heads, int head_dim) {
+  QuantArgs a;
+  a.x = static_cast<const uint16_t*>(x);
+  a.x_token_stride = x_token_stride;
+  a.codes = static_cast<uint8_t*>(codes);
+  a.scales = static_cast<uint16_t*>(scales);
+  a.sink = static_cast<uint16_t*>(sink);
+  a.n_rows = n_tokens * n_heads;
+  a.sink_rows = (sink ? (sink_tokens < n_tokens ? sink_tokens : n_tokens) : 0) * n_heads;
+  a.H = n_heads;
+  a.rows_contig = x_token_stride == static_cast<int64_t>(n_heads) * head_dim;
+  return a;
+}
+
+// n tensors of one shape: one launch of the specialised kernel, or one launch of
+// the generic kernel per tensor.
+static int quantize_tensors(int layout, const GroupMap& map, const QuantArgs* args, int n, int head_dim,
+                            int n_groups, int bits, cudaStream_t st) {
+  if (layout != kLayoutGeneric) {
+    const int64_t tpt = (args[0].n_rows + kQT - 1) / kQT;
+    if (n == 1) {
+      QuantOne o;
+      o.a = args[0];
+      o.tiles_per = tpt;
+      return bits == 4 ? dispatch_fast<4>(layout, o, tpt, st) : dispatch_fast<8>(layout, o, tpt, st);
+    }
+    static thread_local QuantBatch b;  // 6 KB: kept off the stack
+    b.n = n;
+    b.tiles_per = tpt;
+    for (int i = 0; i < n; ++i) b.t[i] = args[i];
+    return bits == 4 ? dispatch_fast<4>(layout, b, tpt * n, st) : dispatch_fast<8>(layout, b, tpt * n, st);
+  }
+  for (int i = 0; i < n; ++i) {
+    const int64_t blocks = (args[i].n_rows + kGW - 1) / kGW;
+    const int grid = static_cast<int>(blocks < num_sms() * 8 ? blocks : num_sms() * 8);
+    quantize_rows_generic<<<grid, kGW * 32, 0, st>>>(args[i], map, head_dim, n_groups, bits);
+    int rc = check_launch("kvq_quantize(generic)");
+    if (rc) return rc;
+  }
+  return KVQ_OK;
+}
+
 extern "C" int kvq_quantize(const void* x, int64_t x_token_stride, void* codes, void* scales, void* sink,
                             int64_t sink_tokens, int64_t n_tokens, int n_heads, int head_dim,
                             const int32_t* chan_band, int n_groups, int bits, void* stream) {
@@ -679,35 +772,41 @@ extern "C" int kvq_quantize(const void* x, int64_t x_token_stride, void* codes, 
   int layout = resolve_layout(chan_band, head_dim, n_groups, &map);
   if (layout < 0) return layout;
   if (n_tokens == 0) return KVQ_OK;
-  KVQ_REQUIRE(x && codes && scales, KVQ_ERR_ARG, "NULL data pointer");
-  KVQ_REQUIRE(x_token_stride >= static_cast<int64_t>(n_heads) * head_dim, KVQ_ERR_ARG,
-              "x_token_stride %lld < n_heads*head_dim", (long long)x_token_stride);
   KVQ_REQUIRE(sink_tokens >= 0, KVQ_ERR_ARG, "negative sink_tokens");
-  KVQ_REQUIRE((reinterpret_cast<uintptr_t>(x) & 15) == 0 && (x_token_stride % 8) == 0, KVQ_ERR_ALIGN,
-              "x must be 16-byte aligned with a token stride that is a multiple of 8 elements");
-  KVQ_REQUIRE((reinterpret_cast<uintptr_t>(codes) & 15) == 0, KVQ_ERR_ALIGN, "codes must be 16-byte aligned");
-  KVQ_REQUIRE((reinterpret_cast<uintptr_t>(scales) & 1) == 0, KVQ_ERR_ALIGN, "scales must be 2-byte aligned");
-  KVQ_REQUIRE(sink == nullptr || (reinterpret_cast<uintptr_t>(sink) & 15) == 0, KVQ_ERR_ALIGN,
-              "sink must be 16-byte aligned");
+  int rc = check_quant_tensor(x, x_token_stride, codes, scales, sink, n_heads, head_dim, 0);
+  if (rc) return rc;
+  rc = require_sm100();
+  if (rc) return rc;
+  const QuantArgs a = quant_args(x, x_token_stride, codes, scales, sink, sink_tokens, n_tokens, n_heads, head_dim);
+  return quantize_tensors(layout, map, &a, 1, head_dim, n_groups, bits, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int kvq_rebuild_layers(int n_tensors, const void* const* x, int64_t x_token_stride, void* const* codes,
+                                  void* const* scales, void* const* sink, int64_t sink_tokens, int64_t n_tokens,
+                                  int n_heads, int head_dim, const int32_t* chan_band, int n_groups, int bits,
+                                  void* stream) {
+  clear_error();
+  KVQ_REQUIRE(n_tensors >= 1 && n_tensors <= kMaxTensors, KVQ_ERR_ARG, "1 to %d tensors, got %d", kMaxTensors,
+              n_tensors);
+  KVQ_REQUIRE(x && codes && scales, KVQ_ERR_ARG, "NULL pointer array");
+  KVQ_REQUIRE(bits == 4 || bits == 8, KVQ_ERR_ARG, "bits must be 4 or 8, got %d", bits);
+  KVQ_REQUIRE(n_tokens >= 0 && n_heads > 0, KVQ_ERR_ARG, "bad shape: n_tokens %lld, n_heads %d",
+              (long long)n_tokens, n_heads);
+  GroupMap map;
+  int layout = resolve_layout(chan_band, head_dim, n_groups, &map);
+  if (layout < 0) return layout;
+  if (n_tokens == 0) return KVQ_OK;
+  KVQ_REQUIRE(sink_tokens >= 0, KVQ_ERR_ARG, "negative sink_tokens");
+  QuantArgs args[kMaxTensors];
+  for (int i = 0; i < n_tensors; ++i) {
+    void* si = sink ? sink[i] : nullptr;
+    int rc = check_quant_tensor(x[i], x_token_stride, codes[i], scales[i], si, n_heads, head_dim, i);
+    if (rc) return rc;
+    args[i] = quant_args(x[i], x_token_stride, codes[i], scales[i], si, sink_tokens, n_tokens, n_heads, head_dim);
+  }
   int rc = require_sm100();
   if (rc) return rc;
-  QuantArgs a;
-  a.x = static_cast<const uint16_t*>(x);
-  a.x_token_stride = x_token_stride;
-  a.codes = static_cast<uint8_t*>(codes);
-  a.scales = static_cast<uint16_t*>(scales);
-  a.sink = static_cast<uint16_t*>(sink);
-  a.n_rows = n_tokens * n_heads;
-  a.sink_rows = (sink ? (sink_tokens < n_tokens ? sink_tokens : n_tokens) : 0) * n_heads;
-  a.H = n_heads;
-  a.rows_contig = x_token_stride == static_cast<int64_t>(n_heads) * head_dim;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (layout != kLayoutGeneric)
-    return bits == 4 ? dispatch_fast<4>(layout, a, st) : dispatch_fast<8>(layout, a, st);
-  const int64_t blocks = (a.n_rows + kGW - 1) / kGW;
-  const int grid = static_cast<int>(blocks < num_sms() * 8 ? blocks : num_sms() * 8);
-  quantize_rows_generic<<<grid, kGW * 32, 0, st>>>(a, map, head_dim, n_groups, bits);
-  return check_launch("kvq_quantize(generic)");
+  return quantize_tensors(layout, map, args, n_tensors, head_dim, n_groups, bits, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int kvq_dequantize(const void* codes, const void* scales, const void* sink, int64_t sink_tokens,

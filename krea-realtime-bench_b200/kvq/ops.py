@@ -89,6 +89,52 @@ def quantize_into(x: torch.Tensor, codes: torch.Tensor, scales: torch.Tensor, ch
     _lib.check(rc, "kvq_quantize")
 
 
+def quantize_layers_into(xs: list[torch.Tensor], codes: list[torch.Tensor], scales: list[torch.Tensor], chan_band,
+                         n_groups: int, bits: int = 4, sinks: list[torch.Tensor | None] | None = None,
+                         sink_tokens: int = 0) -> None:
+    """quantize_into() of n tensors of one shape ([L, H, D] bf16 each, one token
+    stride) in a single launch (kvq_rebuild_layers): the layers x {K, V} of a
+    rebuild or an append. Results are bit-identical to n quantize_into() calls."""
+    n = len(xs)
+    if not 1 <= n <= 96 or len(codes) != n or len(scales) != n or (sinks is not None and len(sinks) != n):
+        raise ValueError("1 to 96 tensors, with one codes/scales (and sink) entry each")
+    dev = _require_cuda(*xs, *codes, *scales, *(sinks or []))
+    L, H, D = xs[0].shape
+    cw = D // 2 if bits == 4 else D
+    stride = None
+    for i in range(n):
+        x = xs[i]
+        if x.dtype != torch.bfloat16 or tuple(x.shape) != (L, H, D):
+            raise ValueError(f"tensor {i}: x must be bf16 {(L, H, D)}")
+        st = _rows_view_ok(x, "x", D)
+        if stride is None:
+            stride = st
+        elif st != stride:
+            raise ValueError("all x must share one token stride")
+        if codes[i].dtype != torch.uint8 or tuple(codes[i].shape) != (L, H, cw) or not codes[i].is_contiguous():
+            raise ValueError(f"tensor {i}: codes must be contiguous uint8 {(L, H, cw)}")
+        if scales[i].dtype != torch.bfloat16 or tuple(scales[i].shape) != (L, H, n_groups) \
+                or not scales[i].is_contiguous():
+            raise ValueError(f"tensor {i}: scales must be contiguous bf16 {(L, H, n_groups)}")
+        sk = sinks[i] if sinks is not None else None
+        if sk is not None and (sk.dtype != torch.bfloat16 or sk.shape[0] < min(sink_tokens, L)
+                               or tuple(sk.shape[1:]) != (H, D) or not sk.is_contiguous()):
+            raise ValueError(f"tensor {i}: sink must be contiguous bf16 [>=sink_tokens, H, D]")
+    cb = _host_map(chan_band)
+    if cb.shape[0] != D:
+        raise ValueError(f"chan_band has {cb.shape[0]} entries, head_dim is {D}")
+    arr = lambda ts: (ctypes.c_void_p * n)(*[_ptr(t) for t in ts])  # noqa: E731
+    sink_arr = arr(sinks) if sinks is not None else None
+    with torch.cuda.device(dev):
+        rc = _lib.load().kvq_rebuild_layers(
+            n, ctypes.cast(arr(xs), ctypes.c_void_p), stride, ctypes.cast(arr(codes), ctypes.c_void_p),
+            ctypes.cast(arr(scales), ctypes.c_void_p),
+            ctypes.cast(sink_arr, ctypes.c_void_p) if sink_arr is not None else None,
+            int(sink_tokens) if sinks is not None else 0, L, H, D, cb.ctypes.data_as(ctypes.c_void_p),
+            int(n_groups), int(bits), _stream(dev))
+    _lib.check(rc, "kvq_rebuild_layers")
+
+
 def dequantize_into(codes: torch.Tensor, scales: torch.Tensor, out: torch.Tensor, chan_band,
                     n_groups: int, bits: int = 4, sink: torch.Tensor | None = None,
                     sink_tokens: int = 0) -> torch.Tensor:

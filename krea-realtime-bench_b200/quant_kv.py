@@ -174,16 +174,7 @@ class QuantKVTensor:
             v = v.to(self.dtype)
         if v.device != self.device:
             v = v.to(self.device)
-        G = len(self.bands)
-        ns = max(0, min(b, self.sink_tokens) - a) if self.sink is not None else 0
-        for i in range(self.n_streams):
-            x = v[i]
-            if x.stride(2) != 1 or x.stride(1) != self.head_dim or x.data_ptr() % 16 or x.stride(0) % 8:
-                x = x.contiguous()
-            rows = self._rows(i, a, b)
-            sink = self.sink[self._sink_rows(i, a, a + ns)] if ns > 0 else None
-            _ops.quantize_into(x, self.packed[rows], self.scales[rows], self.chan_band_host, G,
-                               self.bits, sink=sink, sink_tokens=ns)
+        _write_tensors([(self, v)], a, b)
 
     def read(self, a, b, out=None):
         """Dequantize tokens [a, b) with the sink overlay -> [B, b-a, H, D] bf16."""
@@ -223,6 +214,68 @@ class QuantKVTensor:
         gb = self.storage_bytes() / 1e9
         return (f"QuantKVTensor({tuple(self.logical_shape)}, int{self.bits}, "
                 f"{self.group_mode}, sink={self.sink_tokens}, {gb:.3f} GB)")
+
+
+def _write_tensors(pairs, a, b):
+    """Quantize each value [B, b-a, H, D] into tokens [a, b) of its cache, all
+    (cache, stream) tensors of one shape in as few launches as possible (96
+    tensors per kvq_rebuild_layers launch)."""
+    c0 = pairs[0][0]
+    G = len(c0.bands)
+    ns = max(0, min(b, c0.sink_tokens) - a) if c0.sink is not None else 0
+    xs, codes, scales, sinks = [], [], [], []
+    for cache, v in pairs:
+        for i in range(cache.n_streams):
+            x = v[i]
+            if x.stride(2) != 1 or x.stride(1) != cache.head_dim or x.data_ptr() % 16 or x.stride(0) % 8:
+                x = x.contiguous()
+            rows = cache._rows(i, a, b)
+            xs.append(x)
+            codes.append(cache.packed[rows])
+            scales.append(cache.scales[rows])
+            sinks.append(cache.sink[cache._sink_rows(i, a, a + ns)] if ns > 0 else None)
+    # one token stride per launch: group the tensors by stride
+    by_stride = {}
+    for k, x in enumerate(xs):
+        by_stride.setdefault(x.stride(0), []).append(k)
+    for idx in by_stride.values():
+        for s0 in range(0, len(idx), 96):
+            part = idx[s0:s0 + 96]
+            _ops.quantize_layers_into([xs[k] for k in part], [codes[k] for k in part], [scales[k] for k in part],
+                                      c0.chan_band_host, G, c0.bits,
+                                      sinks=[sinks[k] for k in part] if ns > 0 else None, sink_tokens=ns)
+
+
+def write_layers(caches, values, a: int, b: int) -> None:
+    """caches[i][:, a:b] = values[i] for several caches of one shape, group mode,
+    bits and sink (the 40 layers x {K, V} of a rebuild or an append), with one
+    launch per 96 (cache, stream) tensors instead of one per tensor. Bit-identical
+    to the slice writes (quant_kv.py:201-215 in a loop)."""
+    caches, values = list(caches), list(values)
+    if len(caches) != len(values) or not caches:
+        raise ValueError("one value per cache")
+    c0 = caches[0]
+    key = lambda c: (tuple(c.logical_shape), c.bits, tuple(c.bands), c.sink_tokens, c.sink is None,  # noqa: E731
+                     c.dtype, c.device)
+    if any(key(c) != key(c0) for c in caches):
+        raise ValueError("write_layers needs caches of one shape, group mode, bits and sink")
+    a, b, _ = slice(a, b).indices(c0.n_tokens)
+    if b <= a:
+        return
+    pairs = []
+    for c, v in zip(caches, values):
+        if isinstance(v, QuantKVWindow):
+            v = v.materialize()
+        if v.dim() == 3:
+            v = v.unsqueeze(0)
+        assert v.dim() == 4 and v.shape[0] == c.n_streams and v.shape[1] == b - a, \
+            f"value of shape {tuple(v.shape)} for a write of tokens [{a}, {b}) of {c.n_streams} streams"
+        if v.dtype != c.dtype:
+            v = v.to(c.dtype)
+        if v.device != c.device:
+            v = v.to(c.device)
+        pairs.append((c, v))
+    _write_tensors(pairs, a, b)
 
 
 def _materialize_args(x):
