@@ -108,7 +108,8 @@ KVQ_API int kvq_dequantize(const void* codes, const void* scales, const void* si
  *   lo, hi     window of cache tokens; tokens < sink_tokens come from the sinks
  *   out        bf16 [batch][n_q][n_heads][head_dim], token stride out_token_stride
  *   softmax_scale  <= 0 selects 1/sqrt(head_dim)
- * head_dim 128, int4 K and V, and the five reference group layouts.
+ * head_dim 128; K int4 (k_bits 4) or int8 (k_bits 8, the K8V4 mode of
+ * bench_qkv.py:160) and V int4; the five reference group layouts.
  */
 KVQ_API int kvq_attention(const void* q, int64_t q_token_stride,
                           const void* k_codes, const void* k_scales, const void* k_sink,

@@ -64,7 +64,6 @@ constexpr int BM = 128;   // rows per Q tile
 constexpr int BN = 64;    // KV tokens per tile
 constexpr int D = 128;
 constexpr int NS_KV = 4;  // bf16 K/V tile stages
-constexpr int NS_LD = 4;  // packed-code stages
 constexpr int kThreads = 16 * 32;
 constexpr int kConvWarp0 = 8, kProdWarp = 12, kMmaWarp = 13;  // MMA issuers: warps 13 (Q tile 0), 14 (Q tile 1)
 constexpr uint32_t kTmemCols = 512;
@@ -72,27 +71,39 @@ constexpr uint32_t kColO = 0, kColS = 256;  // S_x buffer u at kColS + 128x + 64
 
 constexpr int kKVTile = BN * D * 2;     // 16 KB: two 8 KB SWIZZLE_128B atoms (d 0-63, 64-127)
 constexpr int kAtom = BN * 128;         // 8 KB
-constexpr int kCodeTile = BN * 64;      // 4 KB: 64 tokens x 64 B, SWIZZLE_64B
-constexpr int kOffK = 0;
-constexpr int kOffV = kOffK + NS_KV * kKVTile;
-constexpr int kOffKC = kOffV + NS_KV * kKVTile;
-constexpr int kOffVC = kOffKC + NS_LD * kCodeTile;
 constexpr int kQTile = BM * D * 2;  // 32 KB: Q_x as two 16 KB SWIZZLE_128B atoms (d 0-63, 64-127)
 constexpr int kQAtom = BM * 128;    // 16 KB
-constexpr int kOffQ = kOffVC + NS_LD * kCodeTile;
-constexpr int kOffBar = kOffQ + 2 * kQTile;
-// barrier indices
-constexpr int bLdFull = 0, bLdEmpty = bLdFull + NS_LD, bKvFull = bLdEmpty + NS_LD, bKvEmpty = bKvFull + NS_KV,
-              bQReady = bKvEmpty + NS_KV, bSFull = bQReady + 2, bPFull = bSFull + 4, bOReady = bPFull + 4,
-              bOFinal = bOReady + 2, bMmaDone = bOFinal + 2, kNumBars = bMmaDone + 2;  // S/P full: 2x + buffer
-static_assert(kOffQ % 1024 == 0, "SWIZZLE_128B operands need 1024-byte alignment");
-constexpr int kOffMisc = kOffBar + kNumBars * 8;
-constexpr int kSmemBytes = kOffMisc + 64 + 1024;  // + alignment slack
+
+// Shared-memory geometry for int4 (KB = 4) or int8 (KB = 8) K codes; V codes
+// are int4. Code tiles are 64 tokens x 64 B (int4, SWIZZLE_64B) or x 128 B
+// (int8, SWIZZLE_128B); int8 K keeps two code stages instead of four so that
+// everything fits the 227 KB of one CTA.
+template <int KB>
+struct Geo {
+  static constexpr int NS_LD = KB == 4 ? 4 : 2;  // packed-code stages
+  static constexpr int kCodeTileK = BN * (KB == 4 ? 64 : 128);
+  static constexpr int kCodeTileV = BN * 64;
+  static constexpr int kOffK = 0;
+  static constexpr int kOffV = kOffK + NS_KV * kKVTile;
+  static constexpr int kOffKC = kOffV + NS_KV * kKVTile;
+  static constexpr int kOffVC = kOffKC + NS_LD * kCodeTileK;
+  static constexpr int kOffQ = kOffVC + NS_LD * kCodeTileV;
+  static constexpr int kOffBar = kOffQ + 2 * kQTile;
+  // barrier indices (S/P full: 2x + buffer)
+  static constexpr int bLdFull = 0, bLdEmpty = bLdFull + NS_LD, bKvFull = bLdEmpty + NS_LD,
+                       bKvEmpty = bKvFull + NS_KV, bQReady = bKvEmpty + NS_KV, bSFull = bQReady + 2,
+                       bPFull = bSFull + 4, bOReady = bPFull + 4, bOFinal = bOReady + 2, bMmaDone = bOFinal + 2,
+                       kNumBars = bMmaDone + 2;
+  static constexpr int kOffMisc = kOffBar + kNumBars * 8;
+  static constexpr int kSmemBytes = kOffMisc + 64 + 1024;  // + alignment slack
+  static_assert(kOffQ % 1024 == 0 && kOffKC % 1024 == 0, "SWIZZLE_128B operands need 1024-byte alignment");
+  static_assert(kSmemBytes <= 227 * 1024, "one CTA per SM must fit");
+};
 
 constexpr int kMaxOut = 8;
 
 struct alignas(64) Args {
-  CUtensorMap tm_kc, tm_vc;  // codes [B*S rows, H*64 B], box 64 x 64, SWIZZLE_64B
+  CUtensorMap tm_kc, tm_vc;  // codes [B*S rows, H*64 B (int8 K: H*128 B)], box 64 (128) x 64, SWIZZLE_64B (128B)
   CUtensorMap tm_ks, tm_vs;  // sinks [B*sink rows, H*128 bf16], box 64 x 64, SWIZZLE_128B
   const uint16_t* q;
   int64_t q_tok_stride, q_batch_stride;
@@ -164,6 +175,38 @@ __device__ __forceinline__ void deq_row(const uint32_t (&w)[16], const uint32_t 
   (st_shared_v4(dst + tile_off(r, Cs), deq8<L, Cs>(w[Cs], w[Cs] >> 4, sp)), ...);
 }
 
+// int8 channels 16C..16C+15 (one 16-byte chunk v of codes q + 128) -> 16 bf16:
+// each byte goes into the low mantissa of 2^23 (exact), minus 2^23 + 128 gives q
+// (exact), times the group's fp32 scale (exact: 8 x 8 significant bits), and one
+// round to bf16 (cvt.rn.bf16x2): the reference's bf16(float(q) * float(scale)).
+// one pair of int8 codes (bytes 2p, 2p+1 of w) times the scale s -> bf16x2
+__device__ __forceinline__ uint32_t deq_pair_i8(uint32_t w, uint32_t sel, float s) {
+  const float2 f = make_float2(__uint_as_float(__byte_perm(w, 0x4B000000u, sel)),
+                               __uint_as_float(__byte_perm(w, 0x4B000000u, sel + 1)));
+  const float2 q = __fadd2_rn(f, make_float2(-8388736.0f, -8388736.0f));
+  const float2 y = __fmul2_rn(q, make_float2(s, s));
+  return pack_bf16x2(y.x, y.y);
+}
+
+template <class L, int C>
+__device__ __forceinline__ void deq16_i8(uint4 v, const float (&sf)[L::G], uint32_t dst, int r) {
+  constexpr int g0 = group_of<L>(16 * C + 0), g1 = group_of<L>(16 * C + 2), g2 = group_of<L>(16 * C + 4),
+                g3 = group_of<L>(16 * C + 6), g4 = group_of<L>(16 * C + 8), g5 = group_of<L>(16 * C + 10),
+                g6 = group_of<L>(16 * C + 12), g7 = group_of<L>(16 * C + 14);
+  st_shared_v4(dst + tile_off(r, 2 * C),
+               make_uint4(deq_pair_i8(v.x, 0x7540u, sf[g0]), deq_pair_i8(v.x, 0x7542u, sf[g1]),
+                          deq_pair_i8(v.y, 0x7540u, sf[g2]), deq_pair_i8(v.y, 0x7542u, sf[g3])));
+  st_shared_v4(dst + tile_off(r, 2 * C + 1),
+               make_uint4(deq_pair_i8(v.z, 0x7540u, sf[g4]), deq_pair_i8(v.z, 0x7542u, sf[g5]),
+                          deq_pair_i8(v.w, 0x7540u, sf[g6]), deq_pair_i8(v.w, 0x7542u, sf[g7])));
+}
+
+template <class L, int... Cs>
+__device__ __forceinline__ void deq_row_i8(uint32_t src, const float (&sf)[L::G], uint32_t dst, int r,
+                                           std::integer_sequence<int, Cs...>) {
+  (deq16_i8<L, Cs>(ld_shared_v4(src + ((Cs ^ (r & 7)) << 4)), sf, dst, r), ...);
+}
+
 // Raw scale words of one row (bf16 pairs, or single bf16 values for odd G).
 template <class L>
 struct ScaleWords {
@@ -212,8 +255,15 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-template <class L>
+template <class L, int KB>
 __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_constant__ Args a) {
+  using GEO = Geo<KB>;
+  constexpr int NS_LD = GEO::NS_LD, kCodeTileK = GEO::kCodeTileK, kCodeTileV = GEO::kCodeTileV;
+  constexpr int kOffK = GEO::kOffK, kOffV = GEO::kOffV, kOffKC = GEO::kOffKC, kOffVC = GEO::kOffVC,
+                kOffQ = GEO::kOffQ, kOffBar = GEO::kOffBar, kOffMisc = GEO::kOffMisc;
+  constexpr int bLdFull = GEO::bLdFull, bLdEmpty = GEO::bLdEmpty, bKvFull = GEO::bKvFull,
+                bKvEmpty = GEO::bKvEmpty, bQReady = GEO::bQReady, bSFull = GEO::bSFull, bPFull = GEO::bPFull,
+                bOReady = GEO::bOReady, bOFinal = GEO::bOFinal, bMmaDone = GEO::bMmaDone;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
@@ -439,19 +489,27 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
 #pragma unroll
         for (int c = 0; c < 16; ++c) st_shared_v4(dst + tile_off(r, c), make_uint4(0, 0, 0, 0));
       } else if (coded) {
-        const uint32_t src = codes_base + ls * kCodeTile + r * 64;
-        uint32_t w[16];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint4 v = ld_shared_v4(src + ((c ^ ((r >> 1) & 3)) << 4));
-          w[4 * c] = v.x;
-          w[4 * c + 1] = v.y;
-          w[4 * c + 2] = v.z;
-          w[4 * c + 3] = v.w;
-        }
         uint32_t sp[L::G];
         scale_pairs<L>(sw, sp);
-        deq_row<L>(w, sp, dst, r, std::make_integer_sequence<int, 16>{});
+        if (KB == 8 && !is_v) {
+          // int8 K row: 128 B of codes, SWIZZLE_128B staging
+          float sf[L::G];
+#pragma unroll
+          for (int g = 0; g < L::G; ++g) sf[g] = __uint_as_float(sp[g] << 16);
+          deq_row_i8<L>(codes_base + ls * kCodeTileK + r * 128, sf, dst, r, std::make_integer_sequence<int, 8>{});
+        } else {
+          const uint32_t src = codes_base + ls * (is_v ? kCodeTileV : kCodeTileK) + r * 64;
+          uint32_t w[16];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint4 v = ld_shared_v4(src + ((c ^ ((r >> 1) & 3)) << 4));
+            w[4 * c] = v.x;
+            w[4 * c + 1] = v.y;
+            w[4 * c + 2] = v.z;
+            w[4 * c + 3] = v.w;
+          }
+          deq_row<L>(w, sp, dst, r, std::make_integer_sequence<int, 16>{});
+        }
       }
       // sink rows were written into the tile by the TMA
       fence_proxy_async_smem();
@@ -474,12 +532,14 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
         if (has_sink && j >= NS_KV &&
             !mbar_wait(&bars[bKvEmpty + ks], ((j / NS_KV) - 1) & 1, abort, &g_attn_status))
           break;
-        const uint32_t bytes = (has_codes ? 2u * kCodeTile : 0u) + (has_sink ? 2u * kKVTile : 0u);
+        const uint32_t bytes = (has_codes ? static_cast<uint32_t>(kCodeTileK + kCodeTileV) : 0u) +
+                               (has_sink ? 2u * kKVTile : 0u);
         mbar_arrive_expect_tx(&bars[bLdFull + ls], bytes);
         if (has_codes) {
           const int row = static_cast<int>(static_cast<int64_t>(b) * a.cache_tokens + t0);
-          tma_load_2d(sbase + kOffKC + ls * kCodeTile, &a.tm_kc, h * 64, row, &bars[bLdFull + ls]);
-          tma_load_2d(sbase + kOffVC + ls * kCodeTile, &a.tm_vc, h * 64, row, &bars[bLdFull + ls]);
+          tma_load_2d(sbase + kOffKC + ls * kCodeTileK, &a.tm_kc, h * (KB == 4 ? 64 : 128), row,
+                      &bars[bLdFull + ls]);
+          tma_load_2d(sbase + kOffVC + ls * kCodeTileV, &a.tm_vc, h * 64, row, &bars[bLdFull + ls]);
         }
         if (has_sink) {
           const int row = static_cast<int>(static_cast<int64_t>(b) * a.sink_tokens + t0);
@@ -593,13 +653,14 @@ static int make_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, ui
   return KVQ_OK;
 }
 
-template <class L>
+template <class L, int KB>
 int launch(const Args& a, int n_ctas, int batch, cudaStream_t st) {
+  constexpr int kSmemBytes = Geo<KB>::kSmemBytes;
   static bool configured[64];
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(attention_kernel<L>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(attention_kernel<L, KB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          kSmemBytes);
     if (e != cudaSuccess) {
       set_error("cudaFuncSetAttribute(attention): %s", cudaGetErrorString(e));
@@ -608,7 +669,7 @@ int launch(const Args& a, int n_ctas, int batch, cudaStream_t st) {
     configured[dev] = true;
   }
   dim3 grid(n_ctas, a.H, batch);
-  attention_kernel<L><<<grid, kThreads, kSmemBytes, st>>>(a);
+  attention_kernel<L, KB><<<grid, kThreads, kSmemBytes, st>>>(a);
   return check_launch("kvq_attention");
 }
 
@@ -624,7 +685,8 @@ static int attention_impl(const void* q, int64_t q_token_stride, const void* k_c
                           int n_heads, int head_dim, const int32_t* chan_band, int n_groups, int k_bits, int v_bits,
                           float softmax_scale, void* stream) {
   KVQ_REQUIRE(head_dim == 128, KVQ_ERR_UNSUPPORTED, "attention supports head_dim 128, got %d", head_dim);
-  KVQ_REQUIRE(k_bits == 4 && v_bits == 4, KVQ_ERR_UNSUPPORTED, "attention reads int4 K and V (got %d/%d bits)",
+  KVQ_REQUIRE((k_bits == 4 || k_bits == 8) && v_bits == 4, KVQ_ERR_UNSUPPORTED,
+              "attention reads int4 or int8 K and int4 V (got %d/%d bits)",
               k_bits, v_bits);
   KVQ_REQUIRE(batch >= 1 && n_heads >= 1 && n_q >= 0 && cache_tokens >= 1, KVQ_ERR_ARG, "bad shape");
   KVQ_REQUIRE(n_heads <= 65535 && batch <= 65535, KVQ_ERR_ARG, "too many heads or streams");
@@ -665,8 +727,10 @@ static int attention_impl(const void* q, int64_t q_token_stride, const void* k_c
   attn::Args a;
   memset(&a, 0, sizeof(a));
   const uint64_t rows = static_cast<uint64_t>(batch) * cache_tokens;
-  rc = attn::make_map(&a.tm_kc, k_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)n_heads * 64,
-                      (uint64_t)n_heads * 64, rows, 64, attn::BN, CU_TENSOR_MAP_SWIZZLE_64B, "k codes");
+  const uint64_t kcw = k_bits == 4 ? 64 : 128;  // K code bytes per (token, head)
+  rc = attn::make_map(&a.tm_kc, k_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)n_heads * kcw,
+                      (uint64_t)n_heads * kcw, rows, static_cast<uint32_t>(kcw), attn::BN,
+                      k_bits == 4 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B, "k codes");
   if (rc) return rc;
   rc = attn::make_map(&a.tm_vc, v_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)n_heads * 64,
                       (uint64_t)n_heads * 64, rows, 64, attn::BN, CU_TENSOR_MAP_SWIZZLE_64B, "v codes");
@@ -701,11 +765,16 @@ static int attention_impl(const void* q, int64_t q_token_stride, const void* k_c
   const int ctas = static_cast<int>((n_q + 2 * attn::BM - 1) / (2 * attn::BM));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   switch (layout) {
-    case kLayoutBands: return attn::launch<LayoutBands>(a, ctas, batch, st);
-    case kLayoutBands2: return attn::launch<LayoutBands2>(a, ctas, batch, st);
-    case kLayoutBands4: return attn::launch<LayoutBands4>(a, ctas, batch, st);
-    case kLayoutBlind32: return attn::launch<LayoutBlind32>(a, ctas, batch, st);
-    case kLayoutBlind64: return attn::launch<LayoutBlind64>(a, ctas, batch, st);
+    case kLayoutBands: return k_bits == 4 ? attn::launch<LayoutBands, 4>(a, ctas, batch, st)
+                                          : attn::launch<LayoutBands, 8>(a, ctas, batch, st);
+    case kLayoutBands2: return k_bits == 4 ? attn::launch<LayoutBands2, 4>(a, ctas, batch, st)
+                                           : attn::launch<LayoutBands2, 8>(a, ctas, batch, st);
+    case kLayoutBands4: return k_bits == 4 ? attn::launch<LayoutBands4, 4>(a, ctas, batch, st)
+                                           : attn::launch<LayoutBands4, 8>(a, ctas, batch, st);
+    case kLayoutBlind32: return k_bits == 4 ? attn::launch<LayoutBlind32, 4>(a, ctas, batch, st)
+                                            : attn::launch<LayoutBlind32, 8>(a, ctas, batch, st);
+    case kLayoutBlind64: return k_bits == 4 ? attn::launch<LayoutBlind64, 4>(a, ctas, batch, st)
+                                            : attn::launch<LayoutBlind64, 8>(a, ctas, batch, st);
     default: break;
   }
   set_error("internal: unhandled layout %d", layout);

@@ -86,7 +86,7 @@ class QuantKVTensor:
     """
 
     def __init__(self, shape, device, dtype=torch.bfloat16, bits=4,
-                 group_mode="bands", sink_tokens=0):
+                 group_mode="bands", sink_tokens=0, lossless_moves=False):
         b, s, h, d = shape
         assert b >= 1, "batch must be >= 1"
         assert bits in (4, 8), "int4 or int8"
@@ -114,6 +114,11 @@ class QuantKVTensor:
         self.sink = (torch.zeros((b * self.sink_tokens, h, d), dtype=dtype, device=dev)
                      if self.sink_tokens else None)
         self.use_kernels = True
+        # off (the reference's semantics): `kv[:, a:b] = kv[:, c:d].clone()` dequantizes
+        # and requantizes the moved tokens (quant_kv.py:217-218, lossy). On: the clone
+        # is a snapshot of the packed rows and the write copies codes and scales
+        # unchanged (the lossless move README.md:259 describes).
+        self.lossless_moves = bool(lossless_moves)
         self.chan_band = _kern.build_chan_band(self.bands, d, dev)
         self.chan_band_host = np.ascontiguousarray(_kern.host_chan_band(self.chan_band))
 
@@ -203,9 +208,25 @@ class QuantKVTensor:
         a, b, _ = sl.indices(self.n_tokens)
         if b <= a:
             return
+        if isinstance(value, PackedBlock) and self.lossless_moves and value.fits(self, b - a):
+            self.write_packed_(a, b, value)
+            return
         if isinstance(value, QuantKVWindow):
             value = value.materialize()
         self.write_(a, b, value)
+
+    def write_packed_(self, a, b, blk):
+        """Tokens [a, b) := the packed rows of blk (codes and scales copied as they
+        are); destination tokens below sink_tokens also get blk's bf16 read values
+        in the sink (exact where blk's rows came from its cache's sink)."""
+        L = b - a
+        ns = max(0, min(b, self.sink_tokens) - a) if self.sink is not None else 0
+        for i in range(self.n_streams):
+            rows = self._rows(i, a, b)
+            self.packed[rows].copy_(blk.packed[i * L:(i + 1) * L])
+            self.scales[rows].copy_(blk.scales[i * L:(i + 1) * L])
+            if ns > 0:
+                self.sink[self._sink_rows(i, a, a + ns)].copy_(blk.read_rows(i, 0, ns))
 
     def clone(self):
         raise RuntimeError("clone() on the whole cache is never called by the runtime")
@@ -324,7 +345,10 @@ class QuantKVWindow:
 
     def clone(self, *a, **kw):
         # the runtime's eviction `kv[:, a:b] = kv[:, c:d].clone()` (quant_kv.py:13): the
-        # reference dequantizes here and requantizes on the write (quant_kv.py:217-218)
+        # reference dequantizes here and requantizes on the write (quant_kv.py:217-218);
+        # with lossless_moves the clone keeps the packed rows instead
+        if self.cache.lossless_moves:
+            return PackedBlock(self.cache, self.lo, self.hi)
         return self.materialize()
 
     @classmethod
@@ -349,6 +373,54 @@ class QuantKVWindow:
         return f"QuantKVWindow({self.cache!r}, tokens [{self.lo}, {self.hi}))"
 
 
+class PackedBlock(QuantKVWindow):
+    """Snapshot of tokens [lo, hi) of a QuantKVTensor in packed form (codes,
+    scales, and the bf16 sink rows the window overlaps), made by clone() of a
+    window of a cache with lossless_moves. Writing it into a slice of a cache of
+    the same format copies the packed rows unchanged; any other use sees the
+    window's bf16 read (dequantize + sink overlay) as of the snapshot."""
+
+    def __init__(self, cache: QuantKVTensor, lo: int, hi: int):
+        super().__init__(cache, lo, hi)
+        L = hi - lo
+        self.packed = torch.cat([cache.packed[cache._rows(i, lo, hi)] for i in range(cache.n_streams)]).clone() \
+            if L > 0 else cache.packed[:0].clone()
+        self.scales = torch.cat([cache.scales[cache._rows(i, lo, hi)] for i in range(cache.n_streams)]).clone() \
+            if L > 0 else cache.scales[:0].clone()
+        self.n_exact = max(0, min(hi, cache.sink_tokens) - lo) if cache.sink is not None else 0
+        self.exact = (torch.stack([cache.sink[cache._sink_rows(i, lo, lo + self.n_exact)]
+                                   for i in range(cache.n_streams)]).clone() if self.n_exact > 0 else None)
+
+    def fits(self, cache: QuantKVTensor, n: int) -> bool:
+        c = self.cache
+        return (n == self.hi - self.lo and cache.bits == c.bits and tuple(cache.bands) == tuple(c.bands)
+                and (cache.n_streams, cache.n_heads, cache.head_dim) == (c.n_streams, c.n_heads, c.head_dim)
+                and cache.device == c.device)
+
+    def read_rows(self, stream: int, a: int, b: int) -> torch.Tensor:
+        """bf16 read of block tokens [a, b) of one stream -> [b-a, H, D]."""
+        c, L = self.cache, self.hi - self.lo
+        out = torch.empty((b - a, c.n_heads, c.head_dim), dtype=c.dtype, device=c.device)
+        if b <= a:
+            return out
+        rows = slice(stream * L + a, stream * L + b)
+        _ops.dequantize_into(self.packed[rows], self.scales[rows], out, c.chan_band_host, len(c.bands), c.bits)
+        e = min(b, self.n_exact)
+        if e > a:
+            out[: e - a].copy_(self.exact[stream, a:e])
+        return out
+
+    def materialize(self) -> torch.Tensor:
+        L = self.hi - self.lo
+        return torch.stack([self.read_rows(i, 0, L) for i in range(self.cache.n_streams)])
+
+    def clone(self, *a, **kw):
+        return self
+
+    def __repr__(self):
+        return f"PackedBlock({self.cache!r}, tokens [{self.lo}, {self.hi}))"
+
+
 def _binop(name):
     def f(self, other):
         return getattr(self.materialize(), name)(_materialize_args(other))
@@ -365,11 +437,14 @@ for _n in ("__neg__", "__abs__", "__float__"):
 QuantKVWindow.__hash__ = object.__hash__
 
 
-def install(pipeline, k_bits=4, v_bits=4, group_mode="bands", sink_frames=0, verbose=True):
+def install(pipeline, k_bits=4, v_bits=4, group_mode="bands", sink_frames=0, verbose=True,
+            lossless_moves=False):
     """Swaps the kv_cache1 allocation for QuantKVTensor (quant_kv.py:228-269).
 
     Patches the instance's `_initialize_kv_cache`; the cross-attention cache is
-    not touched. Returns the original method.
+    not touched. Returns the original method. lossless_moves (off by default,
+    as in the reference) makes the runtime's eviction copy packed rows instead
+    of requantizing them.
     """
     sink_tokens = sink_frames * FRAME_SEQ_LEN
     orig = pipeline._initialize_kv_cache
@@ -391,10 +466,11 @@ def install(pipeline, k_bits=4, v_bits=4, group_mode="bands", sink_frames=0, ver
                 e["local_end_index"] = 0
             return
         cache = []
+        extra = {"lossless_moves": True} if lossless_moves else {}  # the reference's call when off
         for _ in range(pipeline.num_transformer_blocks):
             cache.append({
-                "k": QuantKVTensor(shape, device, dtype, k_bits, group_mode, sink_tokens),
-                "v": QuantKVTensor(shape, device, dtype, v_bits, group_mode, sink_tokens),
+                "k": QuantKVTensor(shape, device, dtype, k_bits, group_mode, sink_tokens, **extra),
+                "v": QuantKVTensor(shape, device, dtype, v_bits, group_mode, sink_tokens, **extra),
                 "global_end_index": 0,
                 "local_end_index": 0,
             })
@@ -423,9 +499,10 @@ def attention(q, k, v, *args, softmax_scale=None, out=None, **kwargs):
     Extra positional/keyword arguments of the upstream signature other than
     softmax_scale are not supported and raise.
     """
-    if not isinstance(k, QuantKVWindow) or not isinstance(v, QuantKVWindow):
+    if not isinstance(k, QuantKVWindow) or not isinstance(v, QuantKVWindow) \
+            or isinstance(k, PackedBlock) or isinstance(v, PackedBlock):
         raise TypeError("attention() takes k and v as QuantKVTensor windows (t[:, lo:hi]); "
-                        "plain tensors have no packed form")
+                        "plain tensors and clones have no packed form in the cache")
     if (k.lo, k.hi) != (v.lo, v.hi):
         raise ValueError(f"k window [{k.lo},{k.hi}) and v window [{v.lo},{v.hi}) differ")
     if args or kwargs:
