@@ -93,7 +93,7 @@ struct Geo {
   static constexpr int bLdFull = 0, bLdEmpty = bLdFull + NS_LD, bKvFull = bLdEmpty + NS_LD,
                        bKvEmpty = bKvFull + NS_KV, bQReady = bKvEmpty + NS_KV, bSFull = bQReady + 2,
                        bPFull = bSFull + 4, bOReady = bPFull + 4, bOFinal = bOReady + 2, bMmaDone = bOFinal + 2,
-                       kNumBars = bMmaDone + 2;
+                       bEpi = bMmaDone + 2, kNumBars = bEpi + 2;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kSmemBytes = kOffMisc + 64 + 1024;  // + alignment slack
   static_assert(kOffQ % 1024 == 0 && kOffKC % 1024 == 0, "SWIZZLE_128B operands need 1024-byte alignment");
@@ -113,6 +113,8 @@ struct alignas(64) Args {
   int Lk, Lq, H;
   uint16_t* out[kMaxOut];  // n_out destinations of identical layout (this GPU's and peers')
   int n_out, out_head0;     // heads of this launch land at heads out_head0.. of each destination
+  int tma_out;              // store through tm_out (one TMA store per Q tile and destination)
+  CUtensorMap tm_out[kMaxOut];  // destination d as [batch][n_q][out_heads * D] bf16, box 64 x 128 x 1, SWIZZLE_128B
   int64_t o_tok_stride, o_batch_stride;
   float scale_log2;
 };
@@ -263,7 +265,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
                 kOffQ = GEO::kOffQ, kOffBar = GEO::kOffBar, kOffMisc = GEO::kOffMisc;
   constexpr int bLdFull = GEO::bLdFull, bLdEmpty = GEO::bLdEmpty, bKvFull = GEO::bKvFull,
                 bKvEmpty = GEO::bKvEmpty, bQReady = GEO::bQReady, bSFull = GEO::bSFull, bPFull = GEO::bPFull,
-                bOReady = GEO::bOReady, bOFinal = GEO::bOFinal, bMmaDone = GEO::bMmaDone;
+                bOReady = GEO::bOReady, bOFinal = GEO::bOFinal, bMmaDone = GEO::bMmaDone, bEpi = GEO::bEpi;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
@@ -298,6 +300,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
     }
     mbar_init(&bars[bMmaDone], 1);
     mbar_init(&bars[bMmaDone + 1], 1);
+    mbar_init(&bars[bEpi], 4);
+    mbar_init(&bars[bEpi + 1], 4);
     *abort = 0;
     fence_mbar_init();
   }
@@ -440,6 +444,40 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
     if (ok && mbar_wait_warp(&bars[bOFinal + x], 0, abort, &g_attn_status)) {
       tc_fence_after();
       const float inv = 1.0f / l;
+      if (a.tma_out) {
+        // Stage the normalised tile in the (no longer read) Q_x buffer, in the
+        // layout of Q (two 64-column SWIZZLE_128B atoms), then one thread stores
+        // it to every destination with TMA: 256-byte rows, asynchronous, so the
+        // traffic to peers drains while the SM runs its next CTA.
+        const uint32_t stage = sbase + kOffQ + x * kQTile;
+#pragma unroll 1
+        for (int k = 0; k < 4; ++k) {
+          uint32_t o[32];
+          tmem_ld32_wait(tO + 32 * k, o);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const int ch = 4 * k + c;  // 16-byte chunk = 8 columns
+            st_shared_v4(stage + (ch >> 3) * kQAtom + r * 128 + (((ch & 7) ^ (r & 7)) << 4),
+                         make_uint4(pack_bf16x2(__uint_as_float(o[8 * c + 0]) * inv, __uint_as_float(o[8 * c + 1]) * inv),
+                                    pack_bf16x2(__uint_as_float(o[8 * c + 2]) * inv, __uint_as_float(o[8 * c + 3]) * inv),
+                                    pack_bf16x2(__uint_as_float(o[8 * c + 4]) * inv, __uint_as_float(o[8 * c + 5]) * inv),
+                                    pack_bf16x2(__uint_as_float(o[8 * c + 6]) * inv, __uint_as_float(o[8 * c + 7]) * inv)));
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[bEpi + x]);
+        if ((warp & 3) == 0 && lane == 0 && mbar_wait(&bars[bEpi + x], 0, abort, &g_attn_status)) {
+          const int xq = (a.out_head0 + h) * D, yq = q0 + x * BM;
+          for (int d = 0; d < a.n_out; ++d) {
+            tma_store_3d(&a.tm_out[d], stage, xq, yq, b);
+            tma_store_3d(&a.tm_out[d], stage + kQAtom, xq + 64, yq, b);
+          }
+          bulk_commit();
+          bulk_wait_read_all();  // the staging buffer must outlive the reads
+        }
+        __syncwarp();
+      } else {
       const int64_t off = b * a.o_batch_stride + static_cast<int64_t>(qi) * a.o_tok_stride +
                           static_cast<int64_t>(a.out_head0 + h) * D;
 #pragma unroll 1
@@ -461,6 +499,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
 #pragma unroll
             for (int c = 0; c < 4; ++c) st_global_v4(a.out[d] + off + 32 * k + 8 * c, v[c]);
         }
+      }
       }
       // No fence: the peer stores drain while the SM runs its next CTA; the
       // consumer orders them by the kernel's completion (stream synchronize on
@@ -653,6 +692,23 @@ static int make_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, ui
   return KVQ_OK;
 }
 
+// 3-D map over an attention output [batch][n_q][heads * D] bf16 (token stride
+// tok elements): box 64 columns x 128 tokens x 1 stream, SWIZZLE_128B; tokens
+// past n_q are clipped by the map, not written into the next stream.
+static int make_out_map(CUtensorMap* m, void* base, uint64_t row_elems, uint64_t tok, uint64_t n_q, uint64_t batch) {
+  EncodeFn fn = encode_fn();
+  KVQ_REQUIRE(fn != nullptr, KVQ_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t dims[3] = {row_elems, n_q, batch};
+  cuuint64_t strides[2] = {tok * 2, tok * 2 * n_q};
+  cuuint32_t box[3] = {64, static_cast<cuuint32_t>(BM), 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  KVQ_REQUIRE(r == CUDA_SUCCESS, KVQ_ERR_CUDA, "cuTensorMapEncodeTiled(output) failed with %d", (int)r);
+  return KVQ_OK;
+}
+
 template <class L, int KB>
 int launch(const Args& a, int n_ctas, int batch, cudaStream_t st) {
   constexpr int kSmemBytes = Geo<KB>::kSmemBytes;
@@ -683,7 +739,7 @@ static int attention_impl(const void* q, int64_t q_token_stride, const void* k_c
                           int64_t cache_tokens, int64_t sink_tokens, int64_t lo, int64_t hi, void* const* outs,
                           int n_outs, int out_head0, int out_heads, int64_t out_token_stride, int batch, int64_t n_q,
                           int n_heads, int head_dim, const int32_t* chan_band, int n_groups, int k_bits, int v_bits,
-                          float softmax_scale, void* stream) {
+                          float softmax_scale, void* stream, bool tma_out) {
   KVQ_REQUIRE(head_dim == 128, KVQ_ERR_UNSUPPORTED, "attention supports head_dim 128, got %d", head_dim);
   KVQ_REQUIRE((k_bits == 4 || k_bits == 8) && v_bits == 4, KVQ_ERR_UNSUPPORTED,
               "attention reads int4 or int8 K and int4 V (got %d/%d bits)",
@@ -756,6 +812,15 @@ static int attention_impl(const void* q, int64_t q_token_stride, const void* k_c
   a.Lq = static_cast<int>(n_q);
   a.H = n_heads;
   for (int d = 0; d < n_outs; ++d) a.out[d] = static_cast<uint16_t*>(outs[d]);
+  a.tma_out = tma_out ? 1 : 0;
+  if (tma_out) {
+    for (int d = 0; d < n_outs; ++d) {
+      rc = attn::make_out_map(&a.tm_out[d], outs[d], static_cast<uint64_t>(out_heads) * head_dim,
+                              static_cast<uint64_t>(out_token_stride), static_cast<uint64_t>(n_q),
+                              static_cast<uint64_t>(batch));
+      if (rc) return rc;
+    }
+  }
   a.n_out = n_outs;
   a.out_head0 = out_head0;
   a.o_tok_stride = out_token_stride;
@@ -795,7 +860,7 @@ extern "C" int kvq_attention(const void* q, int64_t q_token_stride, const void* 
   }
   return attention_impl(q, q_token_stride, k_codes, k_scales, k_sink, v_codes, v_scales, v_sink, cache_tokens,
                         sink_tokens, lo, hi, outs, 1, 0, n_heads, out_token_stride, batch, n_q, n_heads, head_dim,
-                        chan_band, n_groups, k_bits, v_bits, softmax_scale, stream);
+                        chan_band, n_groups, k_bits, v_bits, softmax_scale, stream, false);
 }
 
 extern "C" int kvq_attention_gather(const void* q, int64_t q_token_stride, const void* k_codes,
@@ -808,7 +873,7 @@ extern "C" int kvq_attention_gather(const void* q, int64_t q_token_stride, const
   clear_error();
   return attention_impl(q, q_token_stride, k_codes, k_scales, k_sink, v_codes, v_scales, v_sink, cache_tokens,
                         sink_tokens, lo, hi, outs, n_outs, out_head0, out_heads, out_token_stride, batch, n_q,
-                        n_heads, head_dim, chan_band, n_groups, k_bits, v_bits, softmax_scale, stream);
+                        n_heads, head_dim, chan_band, n_groups, k_bits, v_bits, softmax_scale, stream, true);
 }
 
 extern "C" int kvq_device_status(int reset) {
