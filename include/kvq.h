@@ -120,6 +120,24 @@ KVQ_API int kvq_attention(const void* q, int64_t q_token_stride,
                           int k_bits, int v_bits, float softmax_scale, void* stream);
 
 /*
+ * kvq_attention() that also writes, per (stream, query, head), four fp32 row
+ * statistics of the attention distribution p = softmax(q k^T * scale) to
+ * stats[batch][n_q][n_heads][4] (16-byte aligned): log-sum-exp of the scaled
+ * logits, entropy -sum p ln p (nats), max p, and the mass sum p over cache
+ * tokens below sink_tokens. The reference's attention probe computes the last
+ * three on a sample of queries in fp32 (probe_attention.py:102-121: entropia,
+ * peso_max, massa_ancora; adaptive_reset.py uses them as its spread sensor);
+ * here they come out of the fused kernel for every query.
+ */
+KVQ_API int kvq_attention_stats(const void* q, int64_t q_token_stride,
+                                const void* k_codes, const void* k_scales, const void* k_sink,
+                                const void* v_codes, const void* v_scales, const void* v_sink,
+                                int64_t cache_tokens, int64_t sink_tokens, int64_t lo, int64_t hi,
+                                void* out, int64_t out_token_stride, float* stats, int batch, int64_t n_q,
+                                int n_heads, int head_dim, const int32_t* chan_band, int n_groups,
+                                int k_bits, int v_bits, float softmax_scale, void* stream);
+
+/*
  * kvq_quantize() of the same token range of n_tensors tensors (1..96, e.g. the
  * 40 layers x {K, V} of a window rebuild) in one launch: tensor i reads x[i]
  * and writes codes[i], scales[i] and, for its first sink_tokens tokens,

@@ -114,6 +114,7 @@ struct alignas(64) Args {
   uint16_t* out[kMaxOut];  // n_out destinations of identical layout (this GPU's and peers')
   int n_out, out_head0;     // heads of this launch land at heads out_head0.. of each destination
   int tma_out;              // store through tm_out (one TMA store per Q tile and destination)
+  float* stats;             // STATS kernels: [batch][n_q][n_heads][4] fp32 row statistics
   CUtensorMap tm_out[kMaxOut];  // destination d as [batch][n_q][out_heads * D] bf16, box 64 x 128 x 1, SWIZZLE_128B
   int64_t o_tok_stride, o_batch_stride;
   float scale_log2;
@@ -257,7 +258,7 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-template <class L, int KB>
+template <class L, int KB, bool STATS>
 __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_constant__ Args a) {
   using GEO = Geo<KB>;
   constexpr int NS_LD = GEO::NS_LD, kCodeTileK = GEO::kCodeTileK, kCodeTileV = GEO::kCodeTileV;
@@ -358,6 +359,11 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
       if (lane == 0) mbar_arrive(&bars[bQReady + x]);
     }
     float m = -INFINITY, l = 0.0f;
+    // STATS: with e = 2^(t - m) (t = scaled logit in log2 units), lb = sum e (t - m),
+    // ls = sum of e over sink tokens, mtrue = the row's true max of t (m may lag it
+    // by up to 8). Entropy = ln2 (log2 l - lb / l), max weight = 2^(mtrue - m) / l,
+    // sink mass = ls / l, log-sum-exp = ln2 (m + log2 l).
+    float lb = 0.0f, ls = 0.0f, mtrue = -INFINITY;
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
       const uint32_t tS = tS0 + 64 * (j & 1);
@@ -390,9 +396,14 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
       } else if (mt > m + 8.0f) {
         rescale = true;
         alpha = ex2(m - mt);
+        if (STATS) {
+          lb = alpha * (lb - (mt - m) * l);
+          ls *= alpha;
+        }
         m = mt;
         l *= alpha;
       }
+      if (STATS) mtrue = fmaxf(mtrue, mt);
       if (__any_sync(0xffffffffu, rescale)) {
         // O_x must hold every product up to PV_x(j-1) before it is rescaled:
         // wait for S_x(j+1), issued behind PV_x(j-1) (the next commit into that
@@ -416,14 +427,15 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
         tmem_wait_st();
       }
       const float nm = -m;
-      float sum = 0.0f;
+      float sum = 0.0f, sumb = 0.0f;
       uint32_t pw[32];
 #pragma unroll
       for (int c = 0; c < 16; ++c) {
-        float p0 = ex2(fmaf(__uint_as_float(s0[2 * c]), a.scale_log2, nm));
-        float p1 = ex2(fmaf(__uint_as_float(s0[2 * c + 1]), a.scale_log2, nm));
-        float p2 = ex2(fmaf(__uint_as_float(s1[2 * c]), a.scale_log2, nm));
-        float p3 = ex2(fmaf(__uint_as_float(s1[2 * c + 1]), a.scale_log2, nm));
+        const float x0 = fmaf(__uint_as_float(s0[2 * c]), a.scale_log2, nm);
+        const float x1 = fmaf(__uint_as_float(s0[2 * c + 1]), a.scale_log2, nm);
+        const float x2 = fmaf(__uint_as_float(s1[2 * c]), a.scale_log2, nm);
+        const float x3 = fmaf(__uint_as_float(s1[2 * c + 1]), a.scale_log2, nm);
+        float p0 = ex2(x0), p1 = ex2(x1), p2 = ex2(x2), p3 = ex2(x3);
         if (valid < BN) {
           p0 = (2 * c < valid) ? p0 : 0.0f;
           p1 = (2 * c + 1 < valid) ? p1 : 0.0f;
@@ -431,10 +443,29 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
           p3 = (33 + 2 * c < valid) ? p3 : 0.0f;
         }
         sum += (p0 + p1) + (p2 + p3);
+        if (STATS) sumb += (p0 * x0 + p1 * x1) + (p2 * x2 + p3 * x3);
         pw[c] = pack_bf16x2(p0, p1);
         pw[16 + c] = pack_bf16x2(p2, p3);
       }
       l += sum;
+      if (STATS) {
+        lb += sumb;
+        // columns whose cache token is below sink_tokens
+        const int64_t t0 = a.lo + static_cast<int64_t>(j) * BN;
+        const int ns = static_cast<int>(max(static_cast<int64_t>(0), min(static_cast<int64_t>(valid), a.sink_tokens - t0)));
+        if (ns == valid) {
+          ls += sum;
+        } else if (ns > 0) {
+          // the border tile's sink part, recomputed (one tile per row)
+          float part = 0.0f;
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            if (c < ns) part += ex2(fmaf(__uint_as_float(s0[c]), a.scale_log2, nm));
+            if (32 + c < ns) part += ex2(fmaf(__uint_as_float(s1[c]), a.scale_log2, nm));
+          }
+          ls += part;
+        }
+      }
       tmem_st32(tS, pw);  // P_x(j), 64 bf16 = 32 columns, over S_x(j)
       tmem_wait_st();
       tc_fence_before();
@@ -444,6 +475,16 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
     if (ok && mbar_wait_warp(&bars[bOFinal + x], 0, abort, &g_attn_status)) {
       tc_fence_after();
       const float inv = 1.0f / l;
+      if (STATS && qi < a.Lq) {
+        constexpr float kLn2 = 0.69314718055994531f;
+        const float lg = log2f(l);
+        float4 st;
+        st.x = kLn2 * (m + lg);               // log-sum-exp of the scaled logits (natural log)
+        st.y = kLn2 * (lg - lb * inv);        // entropy of the attention row (nats)
+        st.z = ex2(mtrue - m) * inv;          // largest attention weight
+        st.w = ls * inv;                      // attention mass on the sink tokens
+        *reinterpret_cast<float4*>(a.stats + ((static_cast<int64_t>(b) * a.Lq + qi) * a.H + h) * 4) = st;
+      }
       if (a.tma_out) {
         // Stage the normalised tile in the (no longer read) Q_x buffer, in the
         // layout of Q (two 64-column SWIZZLE_128B atoms), then one thread stores
@@ -709,14 +750,14 @@ static int make_out_map(CUtensorMap* m, void* base, uint64_t row_elems, uint64_t
   return KVQ_OK;
 }
 
-template <class L, int KB>
+template <class L, int KB, bool STATS>
 int launch(const Args& a, int n_ctas, int batch, cudaStream_t st) {
   constexpr int kSmemBytes = Geo<KB>::kSmemBytes;
   static bool configured[64];
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(attention_kernel<L, KB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(attention_kernel<L, KB, STATS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          kSmemBytes);
     if (e != cudaSuccess) {
       set_error("cudaFuncSetAttribute(attention): %s", cudaGetErrorString(e));
@@ -725,8 +766,15 @@ int launch(const Args& a, int n_ctas, int batch, cudaStream_t st) {
     configured[dev] = true;
   }
   dim3 grid(n_ctas, a.H, batch);
-  attention_kernel<L, KB><<<grid, kThreads, kSmemBytes, st>>>(a);
+  attention_kernel<L, KB, STATS><<<grid, kThreads, kSmemBytes, st>>>(a);
   return check_launch("kvq_attention");
+}
+
+template <class L>
+int launch_layout(const Args& a, int n_ctas, int batch, cudaStream_t st, int k_bits, bool stats) {
+  if (k_bits == 4)
+    return stats ? launch<L, 4, true>(a, n_ctas, batch, st) : launch<L, 4, false>(a, n_ctas, batch, st);
+  return stats ? launch<L, 8, true>(a, n_ctas, batch, st) : launch<L, 8, false>(a, n_ctas, batch, st);
 }
 
 }  // namespace attn
@@ -739,7 +787,7 @@ static int attention_impl(const void* q, int64_t q_token_stride, const void* k_c
                           int64_t cache_tokens, int64_t sink_tokens, int64_t lo, int64_t hi, void* const* outs,
                           int n_outs, int out_head0, int out_heads, int64_t out_token_stride, int batch, int64_t n_q,
                           int n_heads, int head_dim, const int32_t* chan_band, int n_groups, int k_bits, int v_bits,
-                          float softmax_scale, void* stream, bool tma_out) {
+                          float softmax_scale, void* stream, bool tma_out, float* stats) {
   KVQ_REQUIRE(head_dim == 128, KVQ_ERR_UNSUPPORTED, "attention supports head_dim 128, got %d", head_dim);
   KVQ_REQUIRE((k_bits == 4 || k_bits == 8) && v_bits == 4, KVQ_ERR_UNSUPPORTED,
               "attention reads int4 or int8 K and int4 V (got %d/%d bits)",
@@ -813,6 +861,9 @@ static int attention_impl(const void* q, int64_t q_token_stride, const void* k_c
   a.H = n_heads;
   for (int d = 0; d < n_outs; ++d) a.out[d] = static_cast<uint16_t*>(outs[d]);
   a.tma_out = tma_out ? 1 : 0;
+  KVQ_REQUIRE(stats == nullptr || (reinterpret_cast<uintptr_t>(stats) & 15) == 0, KVQ_ERR_ALIGN,
+              "stats must be 16-byte aligned");
+  a.stats = stats;
   if (tma_out) {
     for (int d = 0; d < n_outs; ++d) {
       rc = attn::make_out_map(&a.tm_out[d], outs[d], static_cast<uint64_t>(out_heads) * head_dim,
@@ -830,16 +881,11 @@ static int attention_impl(const void* q, int64_t q_token_stride, const void* k_c
   const int ctas = static_cast<int>((n_q + 2 * attn::BM - 1) / (2 * attn::BM));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   switch (layout) {
-    case kLayoutBands: return k_bits == 4 ? attn::launch<LayoutBands, 4>(a, ctas, batch, st)
-                                          : attn::launch<LayoutBands, 8>(a, ctas, batch, st);
-    case kLayoutBands2: return k_bits == 4 ? attn::launch<LayoutBands2, 4>(a, ctas, batch, st)
-                                           : attn::launch<LayoutBands2, 8>(a, ctas, batch, st);
-    case kLayoutBands4: return k_bits == 4 ? attn::launch<LayoutBands4, 4>(a, ctas, batch, st)
-                                           : attn::launch<LayoutBands4, 8>(a, ctas, batch, st);
-    case kLayoutBlind32: return k_bits == 4 ? attn::launch<LayoutBlind32, 4>(a, ctas, batch, st)
-                                            : attn::launch<LayoutBlind32, 8>(a, ctas, batch, st);
-    case kLayoutBlind64: return k_bits == 4 ? attn::launch<LayoutBlind64, 4>(a, ctas, batch, st)
-                                            : attn::launch<LayoutBlind64, 8>(a, ctas, batch, st);
+    case kLayoutBands: return attn::launch_layout<LayoutBands>(a, ctas, batch, st, k_bits, stats != nullptr);
+    case kLayoutBands2: return attn::launch_layout<LayoutBands2>(a, ctas, batch, st, k_bits, stats != nullptr);
+    case kLayoutBands4: return attn::launch_layout<LayoutBands4>(a, ctas, batch, st, k_bits, stats != nullptr);
+    case kLayoutBlind32: return attn::launch_layout<LayoutBlind32>(a, ctas, batch, st, k_bits, stats != nullptr);
+    case kLayoutBlind64: return attn::launch_layout<LayoutBlind64>(a, ctas, batch, st, k_bits, stats != nullptr);
     default: break;
   }
   set_error("internal: unhandled layout %d", layout);
@@ -860,7 +906,25 @@ extern "C" int kvq_attention(const void* q, int64_t q_token_stride, const void* 
   }
   return attention_impl(q, q_token_stride, k_codes, k_scales, k_sink, v_codes, v_scales, v_sink, cache_tokens,
                         sink_tokens, lo, hi, outs, 1, 0, n_heads, out_token_stride, batch, n_q, n_heads, head_dim,
-                        chan_band, n_groups, k_bits, v_bits, softmax_scale, stream, false);
+                        chan_band, n_groups, k_bits, v_bits, softmax_scale, stream, false, nullptr);
+}
+
+extern "C" int kvq_attention_stats(const void* q, int64_t q_token_stride, const void* k_codes,
+                                   const void* k_scales, const void* k_sink, const void* v_codes,
+                                   const void* v_scales, const void* v_sink, int64_t cache_tokens,
+                                   int64_t sink_tokens, int64_t lo, int64_t hi, void* out, int64_t out_token_stride,
+                                   float* stats, int batch, int64_t n_q, int n_heads, int head_dim,
+                                   const int32_t* chan_band, int n_groups, int k_bits, int v_bits,
+                                   float softmax_scale, void* stream) {
+  clear_error();
+  void* outs[1] = {out};
+  if (n_q > 0 && (!out || !stats)) {
+    set_error("NULL output or stats pointer");
+    return KVQ_ERR_ARG;
+  }
+  return attention_impl(q, q_token_stride, k_codes, k_scales, k_sink, v_codes, v_scales, v_sink, cache_tokens,
+                        sink_tokens, lo, hi, outs, 1, 0, n_heads, out_token_stride, batch, n_q, n_heads, head_dim,
+                        chan_band, n_groups, k_bits, v_bits, softmax_scale, stream, false, stats);
 }
 
 extern "C" int kvq_attention_gather(const void* q, int64_t q_token_stride, const void* k_codes,
@@ -873,7 +937,7 @@ extern "C" int kvq_attention_gather(const void* q, int64_t q_token_stride, const
   clear_error();
   return attention_impl(q, q_token_stride, k_codes, k_scales, k_sink, v_codes, v_scales, v_sink, cache_tokens,
                         sink_tokens, lo, hi, outs, n_outs, out_head0, out_heads, out_token_stride, batch, n_q,
-                        n_heads, head_dim, chan_band, n_groups, k_bits, v_bits, softmax_scale, stream, true);
+                        n_heads, head_dim, chan_band, n_groups, k_bits, v_bits, softmax_scale, stream, true, nullptr);
 }
 
 extern "C" int kvq_device_status(int reset) {

@@ -28,6 +28,8 @@ SIGNATURES = {
     "kvq_dequantize": (_i32, [_p, _p, _p, _i64, _p, _i64, _i64, _i32, _i32, _p, _i32, _i32, _p]),
     "kvq_attention": (_i32, [_p, _i64, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _i64, _i32, _i64,
                              _i32, _i32, _p, _i32, _i32, _i32, _f32, _p]),
+    "kvq_attention_stats": (_i32, [_p, _i64, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _i64, _p, _i32,
+                                   _i64, _i32, _i32, _p, _i32, _i32, _i32, _f32, _p]),
     "kvq_rebuild_layers": (_i32, [_i32, _p, _i64, _p, _p, _p, _i64, _i64, _i32, _i32, _p, _i32, _i32, _p]),
     "kvq_attention_gather": (_i32, [_p, _i64, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _i32, _i32, _i32,
                                     _i64, _i32, _i64, _i32, _i32, _p, _i32, _i32, _i32, _f32, _p]),

@@ -165,9 +165,11 @@ def dequantize_into(codes: torch.Tensor, scales: torch.Tensor, out: torch.Tensor
 
 
 def attention_packed(q: torch.Tensor, k_cache, v_cache, lo: int, hi: int, out: torch.Tensor | None = None,
-                     softmax_scale: float | None = None) -> torch.Tensor:
+                     softmax_scale: float | None = None, stats: torch.Tensor | None = None) -> torch.Tensor:
     """Fused int4-KV attention of q [B, Lq, H, D] bf16 over tokens [lo, hi) of two
-    QuantKVTensor caches (same shape, group mode and sink). Returns out [B, Lq, H, D] bf16."""
+    QuantKVTensor caches (same shape, group mode and sink). Returns out [B, Lq, H, D] bf16.
+    With stats (fp32 [B, Lq, H, 4], contiguous) the kernel also writes per row:
+    log-sum-exp, entropy (nats), max weight and the mass on the sink tokens."""
     dev = _require_cuda(q, k_cache.packed, v_cache.packed, out)
     if q.dtype != torch.bfloat16 or q.dim() != 4:
         raise TypeError("q must be a [B, Lq, H, D] bfloat16 tensor")
@@ -186,13 +188,19 @@ def attention_packed(q: torch.Tensor, k_cache, v_cache, lo: int, hi: int, out: t
           or out.stride(2) != D or out.stride(0) != Lq * out.stride(1)):
         raise ValueError("out must be bf16 [B, Lq, H, D] with contiguous heads and a uniform token stride")
     cb = _host_map(k_cache.chan_band_host)
-    with torch.cuda.device(dev):
-        rc = _lib.load().kvq_attention(
-            _ptr(q), q.stride(1), _ptr(k_cache.packed), _ptr(k_cache.scales), _ptr(k_cache.sink),
-            _ptr(v_cache.packed), _ptr(v_cache.scales), _ptr(v_cache.sink), k_cache.n_tokens,
-            k_cache.sink_tokens if k_cache.sink is not None else 0, int(lo), int(hi), _ptr(out), out.stride(1),
-            B, Lq, H, D, cb.ctypes.data_as(ctypes.c_void_p), len(k_cache.bands), k_cache.bits, v_cache.bits,
+    common = (_ptr(q), q.stride(1), _ptr(k_cache.packed), _ptr(k_cache.scales), _ptr(k_cache.sink),
+              _ptr(v_cache.packed), _ptr(v_cache.scales), _ptr(v_cache.sink), k_cache.n_tokens,
+              k_cache.sink_tokens if k_cache.sink is not None else 0, int(lo), int(hi), _ptr(out), out.stride(1))
+    tail = (B, Lq, H, D, cb.ctypes.data_as(ctypes.c_void_p), len(k_cache.bands), k_cache.bits, v_cache.bits,
             float(softmax_scale) if softmax_scale else 0.0, _stream(dev))
+    with torch.cuda.device(dev):
+        if stats is None:
+            rc = _lib.load().kvq_attention(*common, *tail)
+        else:
+            _require_cuda(stats)
+            if stats.dtype != torch.float32 or tuple(stats.shape) != (B, Lq, H, 4) or not stats.is_contiguous():
+                raise ValueError(f"stats must be contiguous float32 {(B, Lq, H, 4)}")
+            rc = _lib.load().kvq_attention_stats(*common, _ptr(stats), *tail)
     _lib.check(rc, "kvq_attention")
     return out
 

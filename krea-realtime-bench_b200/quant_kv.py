@@ -237,6 +237,24 @@ class QuantKVTensor:
                 f"{self.group_mode}, sink={self.sink_tokens}, {gb:.3f} GB)")
 
 
+def attention_stats(q, k, v, softmax_scale=None):
+    """attention() plus per-row statistics of the attention distribution, from the
+    same fused kernel: returns (out [B, Lq, H, D] bf16, stats [B, Lq, H, 4] fp32)
+    with stats[..., 0] = log-sum-exp of the scaled logits, [..., 1] = entropy
+    -sum p ln p (nats), [..., 2] = max p, [..., 3] = attention mass on the sink
+    tokens. The reference's probe computes entropia / peso_max / massa_ancora the
+    same way on a sample of queries (probe_attention.py:102-121)."""
+    if not isinstance(k, QuantKVWindow) or not isinstance(v, QuantKVWindow) \
+            or isinstance(k, PackedBlock) or isinstance(v, PackedBlock):
+        raise TypeError("attention_stats() takes k and v as QuantKVTensor windows (t[:, lo:hi])")
+    if (k.lo, k.hi) != (v.lo, v.hi):
+        raise ValueError(f"k window [{k.lo},{k.hi}) and v window [{v.lo},{v.hi}) differ")
+    B, Lq, H, _ = q.shape
+    stats = torch.empty((B, Lq, H, 4), dtype=torch.float32, device=k.cache.device)
+    out = _ops.attention_packed(q, k.cache, v.cache, k.lo, k.hi, softmax_scale=softmax_scale, stats=stats)
+    return out, stats
+
+
 def _write_tensors(pairs, a, b):
     """Quantize each value [B, b-a, H, D] into tokens [a, b) of its cache, all
     (cache, stream) tensors of one shape in as few launches as possible (96

@@ -181,3 +181,36 @@ def test_attention_rejects_int8_v():
     q = synth.make_q(1, 16, 2, seed=1).cuda()
     with pytest.raises(ValueError):
         quant_kv.attention(q, tk[:, 0:256], tv[:, 0:256])
+
+
+@pytest.mark.parametrize("B,S,H,Lq,lo,hi,sink,mode", [(1, 4680, 8, 600, 0, 4680, 1560, "bands4"),
+                                                      (2, 900, 3, 333, 100, 877, 300, "bands"),
+                                                      (1, 700, 2, 129, 0, 700, 0, "blind64")])
+def test_attention_stats_match_fp32_softmax(B, S, H, Lq, lo, hi, sink, mode):
+    """The side output against the reference probe's fp32 arithmetic on the same
+    (dequantized) window: entropy, max weight and sink mass (probe_attention.py:
+    102-121, without the probe's 1e-9 in the log), plus the log-sum-exp."""
+    import quant_kv
+    from kvq import synth
+    tk, tv, kb, vb = _make_caches(B, S, H, mode, sink, seed=41)
+    q = synth.make_q(B, Lq, H, seed=43)
+    out, st = quant_kv.attention_stats(q.cuda(), tk[:, lo:hi], tv[:, lo:hi])
+    plain = quant_kv.attention(q.cuda(), tk[:, lo:hi], tv[:, lo:hi])
+    assert torch.equal(out.view(torch.int16), plain.view(torch.int16))      # same attention result
+    bands = ko.band_edges(128, mode)
+    kw = np.stack([_oracle_window(kb[b], bands, sink, lo, hi) for b in range(B)])
+    qf = torch.from_numpy(ko.bf16_to_f32(_u16(q))).double()
+    kf = torch.from_numpy(ko.bf16_to_f32(kw)).double()
+    logits = torch.einsum("bqhd,bkhd->bqhk", qf, kf) / math.sqrt(128)
+    lse = torch.logsumexp(logits, -1)
+    p = torch.softmax(logits, -1)
+    ent = -(p * torch.log(p.clamp_min(1e-300))).sum(-1)
+    pmax = p.max(-1).values
+    ns = max(0, min(hi, sink) - lo)
+    anchor = p[..., :ns].sum(-1)
+    got = st.double().cpu()
+    assert (got[..., 0] - lse).abs().max() < 2e-3
+    assert (got[..., 1] - ent).abs().max() < 2e-3
+    assert (got[..., 2] - pmax).abs().max() < 2e-3
+    assert (got[..., 3] - anchor).abs().max() < 2e-3
+    assert quant_kv._ops.device_status() == 0
