@@ -490,6 +490,24 @@ def run_extras(dev, peaks):
         del xs, cs, ss, outs
         torch.cuda.empty_cache()
 
+    # the append of one block of keys before their rotary embedding (fused rotate + quantize)
+    from kvq import rope
+    fr = rope.freqs(1024, device=dev)
+    pos = rope.grid_positions(0, LK, device=dev)
+    xs = [synth.make_k(LK, H_TOTAL, seed=60 + i, device=dev) for i in range(4)]
+    cs = [torch.empty((LK, H_TOTAL, D // 2), dtype=torch.uint8, device=dev) for _ in range(4)]
+    ss = [torch.empty((LK, H_TOTAL, G), dtype=torch.bfloat16, device=dev) for _ in range(4)]
+
+    def fr_q(i):
+        j = i % 4
+        ops.rope_quantize_into(xs[j], cs[j], ss[j], cb, G, 4, fr, pos)
+    ms = _time_events(fr_q, 20)
+    byts = LK * H_TOTAL * quant_bytes_per_row(G)
+    res["rope_quantize_append_block_4680_per_tensor"] = {
+        "gbs": byts / (statistics.median(ms) / 1e3) / 1e9, "ms": statistics.median(ms), "bytes": byts}
+    del xs, cs, ss
+    torch.cuda.empty_cache()
+
     # the append of one block to all 40 layers x {K, V} in one launch (kvq_rebuild_layers)
     nt = 80
     xs = [synth.make_k(LK, H_TOTAL, seed=700 + (i % 8), device=dev) for i in range(8)]

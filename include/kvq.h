@@ -138,6 +138,23 @@ KVQ_API int kvq_attention_stats(const void* q, int64_t q_token_stride,
                                 int k_bits, int v_bits, float softmax_scale, void* stream);
 
 /*
+ * kvq_quantize() of keys before their rotary embedding: each row is rotated
+ * first, exactly as the upstream runtime does before its cache write (Wan's
+ * rope_apply, not vendored; band split quant_kv.py:26-31): channel pairs
+ * (2i, 2i+1) as complex128 times freqs[positions[t][a(i)]][i] = (cos, sin)
+ * (a(i) = 0/1/2 for pairs [0,22)/[22,43)/[43,64): frame/height/width axis),
+ * rounded to fp32 and then to bf16; then quantized, and the sink rows receive the
+ * rotated bf16 values. freqs: device float64 [max_pos][64][2] (16-byte aligned);
+ * positions: device int32 [n_tokens][3] (values outside [0, max_pos) clamp).
+ * head_dim 128 and the five specialised group layouts. Replaces the separate
+ * rotary kernel and cache write (quant_kv.py:12) of an append.
+ */
+KVQ_API int kvq_rope_quantize(const void* x, int64_t x_token_stride, void* codes, void* scales, void* sink,
+                              int64_t sink_tokens, int64_t n_tokens, int n_heads, int head_dim,
+                              const int32_t* chan_band, int n_groups, int bits, const double* freqs,
+                              int max_pos, const int32_t* positions, void* stream);
+
+/*
  * kvq_quantize() of the same token range of n_tensors tensors (1..96, e.g. the
  * 40 layers x {K, V} of a window rebuild) in one launch: tensor i reads x[i]
  * and writes codes[i], scales[i] and, for its first sink_tokens tokens,

@@ -43,6 +43,11 @@ struct QuantArgs {
   int64_t sink_rows;  // rows of x that are also copied to sink
   int H;
   int rows_contig;  // x_token_stride == H * D
+  // fused rotary embedding (kvq_rope_quantize): pair i of a row rotates by
+  // freqs[pos[t][axis(i)]][i] = (cos, sin), fp64, axis 0/1/2 for pairs [0,22)/[22,43)/[43,64)
+  const double2* freqs;
+  const int* pos;  // [n_tokens][3]
+  int max_pos;
 };
 
 // Up to kMaxTensors tensors of identical shape quantized by one launch (the
@@ -244,7 +249,38 @@ constexpr int pipe_smem_bytes() {
 // Persistent CTAs walk the 128-row tiles with a grid stride; each thread keeps
 // the next kStages-1 tiles' input in flight (cp.async, 16 bytes per copy, into
 // the XOR-swizzled layout) while it quantizes its row of the current tile.
-template <class L, int BITS, class P>
+// Rotary embedding of one staged row in place (16 chunks of 4 bf16 pairs, XOR-
+// swizzled), as the upstream complex128 product (x0 + i x1)(cos + i sin) =
+// (x0 cos - x1 sin) + i (x0 sin + x1 cos), rounded to fp32 and then to bf16 (the
+// upstream result is float32 and the cache stores bf16). Products and sums are
+// separate IEEE fp64 operations. One chunk at a time keeps register use low.
+__device__ __forceinline__ uint32_t rope_pair(uint32_t w, double2 cs) {
+  const double x0 = static_cast<double>(__uint_as_float(w << 16));
+  const double x1 = static_cast<double>(__uint_as_float(w & 0xFFFF0000u));
+  const double y0 = __dsub_rn(__dmul_rn(x0, cs.x), __dmul_rn(x1, cs.y));
+  const double y1 = __dadd_rn(__dmul_rn(x0, cs.y), __dmul_rn(x1, cs.x));
+  return pack_bf16x2(__double2float_rn(y0), __double2float_rn(y1));
+}
+
+__device__ __forceinline__ void rope_row(const QuantArgs& a, int64_t token, uint4* trow, int r) {
+  const int* pp = a.pos + token * 3;
+  const int p0 = min(max(pp[0], 0), a.max_pos - 1), p1 = min(max(pp[1], 0), a.max_pos - 1),
+            p2 = min(max(pp[2], 0), a.max_pos - 1);  // out-of-range positions clamp
+#pragma unroll 4
+  for (int c = 0; c < 16; ++c) {
+    uint4 v = trow[c ^ (r & 7)];
+    uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int i = 4 * c + k;  // pair index = channels (2i, 2i+1)
+      const int p = i < 22 ? p0 : (i < 43 ? p1 : p2);
+      w[k] = rope_pair(w[k], a.freqs[static_cast<int64_t>(p) * 64 + i]);
+    }
+    trow[c ^ (r & 7)] = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+template <class L, int BITS, class P, bool ROPE>
 __global__ void __launch_bounds__(kQT, 3) quantize_rows_pipe(const __grid_constant__ P bt, int64_t n_tiles) {
   using C = QuantConsts<BITS>;
   constexpr int G = L::G;
@@ -310,6 +346,9 @@ __global__ void __launch_bounds__(kQT, 3) quantize_rows_pipe(const __grid_consta
     advance(ci, cl);
     const int nrows = static_cast<int>(min(static_cast<int64_t>(kQT), a.n_rows - row0));
     if (tid < nrows) {
+      // the rotated row replaces the staged input: the loads below, the exact-divide
+      // fix-up and the sink copy all read the stage
+      if constexpr (ROPE) rope_row(a, (row0 + tid) / a.H, sm_in + stage * kQT * 16 + tid * 16, tid);
       uint32_t w[64];
 #pragma unroll
       for (int c = 0; c < 16; ++c) {
@@ -639,7 +678,7 @@ static int num_sms() {
   return sms[dev];
 }
 
-template <class L, int BITS, class P>
+template <class L, int BITS, class P, bool ROPE = false>
 static int launch_fast(const P& b, int64_t tiles, cudaStream_t st) {
   constexpr int smem = pipe_smem_bytes<L, BITS>();
   constexpr int per_sm = (227 * 1024) / smem < 3 ? (227 * 1024) / smem : 3;  // 3 for int4, 2 for int8
@@ -649,8 +688,8 @@ static int launch_fast(const P& b, int64_t tiles, cudaStream_t st) {
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(quantize_rows_pipe<L, BITS, P>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         smem);
+    cudaError_t e = cudaFuncSetAttribute(quantize_rows_pipe<L, BITS, P, ROPE>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) {
       set_error("cudaFuncSetAttribute(quantize): %s", cudaGetErrorString(e));
       return KVQ_ERR_CUDA;
@@ -659,18 +698,18 @@ static int launch_fast(const P& b, int64_t tiles, cudaStream_t st) {
   }
   const int64_t cap = static_cast<int64_t>(per_sm) * num_sms();
   const unsigned grid = static_cast<unsigned>(tiles < cap ? tiles : cap);
-  quantize_rows_pipe<L, BITS, P><<<grid, kQT, smem, st>>>(b, tiles);
+  quantize_rows_pipe<L, BITS, P, ROPE><<<grid, kQT, smem, st>>>(b, tiles);
   return check_launch("kvq_quantize");
 }
 
-template <int BITS, class P>
+template <int BITS, class P, bool ROPE = false>
 static int dispatch_fast(int layout, const P& a, int64_t tiles, cudaStream_t st) {
   switch (layout) {
-    case kLayoutBands: return launch_fast<LayoutBands, BITS>(a, tiles, st);
-    case kLayoutBands2: return launch_fast<LayoutBands2, BITS>(a, tiles, st);
-    case kLayoutBands4: return launch_fast<LayoutBands4, BITS>(a, tiles, st);
-    case kLayoutBlind32: return launch_fast<LayoutBlind32, BITS>(a, tiles, st);
-    case kLayoutBlind64: return launch_fast<LayoutBlind64, BITS>(a, tiles, st);
+    case kLayoutBands: return launch_fast<LayoutBands, BITS, P, ROPE>(a, tiles, st);
+    case kLayoutBands2: return launch_fast<LayoutBands2, BITS, P, ROPE>(a, tiles, st);
+    case kLayoutBands4: return launch_fast<LayoutBands4, BITS, P, ROPE>(a, tiles, st);
+    case kLayoutBlind32: return launch_fast<LayoutBlind32, BITS, P, ROPE>(a, tiles, st);
+    case kLayoutBlind64: return launch_fast<LayoutBlind64, BITS, P, ROPE>(a, tiles, st);
     default: break;
   }
   set_error("internal: no specialised kernel for layout %d", layout);
@@ -730,6 +769,9 @@ static QuantArgs quant_args(const void* x, int64_t x_token_stride, void* codes, 
   a.sink_rows = (sink ? (sink_tokens < n_tokens ? sink_tokens : n_tokens) : 0) * n_heads;
   a.H = n_heads;
   a.rows_contig = x_token_stride == static_cast<int64_t>(n_heads) * head_dim;
+  a.freqs = nullptr;
+  a.pos = nullptr;
+  a.max_pos = 0;
   return a;
 }
 
@@ -779,6 +821,41 @@ extern "C" int kvq_quantize(const void* x, int64_t x_token_stride, void* codes, 
   if (rc) return rc;
   const QuantArgs a = quant_args(x, x_token_stride, codes, scales, sink, sink_tokens, n_tokens, n_heads, head_dim);
   return quantize_tensors(layout, map, &a, 1, head_dim, n_groups, bits, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int kvq_rope_quantize(const void* x, int64_t x_token_stride, void* codes, void* scales, void* sink,
+                                 int64_t sink_tokens, int64_t n_tokens, int n_heads, int head_dim,
+                                 const int32_t* chan_band, int n_groups, int bits, const double* freqs, int max_pos,
+                                 const int32_t* positions, void* stream) {
+  clear_error();
+  KVQ_REQUIRE(bits == 4 || bits == 8, KVQ_ERR_ARG, "bits must be 4 or 8, got %d", bits);
+  KVQ_REQUIRE(n_tokens >= 0 && n_heads > 0, KVQ_ERR_ARG, "bad shape: n_tokens %lld, n_heads %d",
+              (long long)n_tokens, n_heads);
+  KVQ_REQUIRE(head_dim == 128, KVQ_ERR_UNSUPPORTED, "the fused rotary embedding is for head_dim 128, got %d",
+              head_dim);
+  GroupMap map;
+  int layout = resolve_layout(chan_band, head_dim, n_groups, &map);
+  if (layout < 0) return layout;
+  KVQ_REQUIRE(layout != kLayoutGeneric, KVQ_ERR_UNSUPPORTED,
+              "the fused rotary embedding supports the bands, bands2, bands4, blind32 and blind64 group maps");
+  if (n_tokens == 0) return KVQ_OK;
+  KVQ_REQUIRE(sink_tokens >= 0, KVQ_ERR_ARG, "negative sink_tokens");
+  KVQ_REQUIRE(freqs && positions && max_pos > 0, KVQ_ERR_ARG, "NULL freqs or positions, or max_pos < 1");
+  KVQ_REQUIRE((reinterpret_cast<uintptr_t>(freqs) & 15) == 0 && (reinterpret_cast<uintptr_t>(positions) & 3) == 0,
+              KVQ_ERR_ALIGN, "freqs must be 16-byte and positions 4-byte aligned");
+  int rc = check_quant_tensor(x, x_token_stride, codes, scales, sink, n_heads, head_dim, 0);
+  if (rc) return rc;
+  rc = require_sm100();
+  if (rc) return rc;
+  QuantOne o;
+  o.a = quant_args(x, x_token_stride, codes, scales, sink, sink_tokens, n_tokens, n_heads, head_dim);
+  o.a.freqs = reinterpret_cast<const double2*>(freqs);
+  o.a.pos = positions;
+  o.a.max_pos = max_pos;
+  o.tiles_per = (o.a.n_rows + kQT - 1) / kQT;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return bits == 4 ? dispatch_fast<4, QuantOne, true>(layout, o, o.tiles_per, st)
+                   : dispatch_fast<8, QuantOne, true>(layout, o, o.tiles_per, st);
 }
 
 extern "C" int kvq_rebuild_layers(int n_tensors, const void* const* x, int64_t x_token_stride, void* const* codes,

@@ -30,6 +30,7 @@ SIGNATURES = {
                              _i32, _i32, _p, _i32, _i32, _i32, _f32, _p]),
     "kvq_attention_stats": (_i32, [_p, _i64, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _i64, _p, _i32,
                                    _i64, _i32, _i32, _p, _i32, _i32, _i32, _f32, _p]),
+    "kvq_rope_quantize": (_i32, [_p, _i64, _p, _p, _p, _i64, _i64, _i32, _i32, _p, _i32, _i32, _p, _i32, _p, _p]),
     "kvq_rebuild_layers": (_i32, [_i32, _p, _i64, _p, _p, _p, _i64, _i64, _i32, _i32, _p, _i32, _i32, _p]),
     "kvq_attention_gather": (_i32, [_p, _i64, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _i32, _i32, _i32,
                                     _i64, _i32, _i64, _i32, _i32, _p, _i32, _i32, _i32, _f32, _p]),

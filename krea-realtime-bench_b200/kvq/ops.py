@@ -89,6 +89,40 @@ def quantize_into(x: torch.Tensor, codes: torch.Tensor, scales: torch.Tensor, ch
     _lib.check(rc, "kvq_quantize")
 
 
+def rope_quantize_into(x: torch.Tensor, codes: torch.Tensor, scales: torch.Tensor, chan_band, n_groups: int,
+                       bits: int, freqs: torch.Tensor, positions: torch.Tensor, sink: torch.Tensor | None = None,
+                       sink_tokens: int = 0) -> None:
+    """quantize_into() of pre-rotary keys x [L, H, 128]: rotated in the kernel by
+    freqs [P, 64, 2] float64 (kvq.rope.freqs) at positions [L, 3] int32 (frame,
+    height, width; kvq.rope.grid_positions), as the upstream runtime rotates
+    before its cache write (kvq_rope_quantize)."""
+    dev = _require_cuda(x, codes, scales, sink, freqs, positions)
+    if x.dtype != torch.bfloat16:
+        raise TypeError(f"x must be bfloat16, got {x.dtype}")
+    L, H, D = x.shape
+    xs = _rows_view_ok(x, "x", D)
+    cw = D // 2 if bits == 4 else D
+    if codes.dtype != torch.uint8 or tuple(codes.shape) != (L, H, cw) or not codes.is_contiguous():
+        raise ValueError(f"codes must be contiguous uint8 {(L, H, cw)}")
+    if scales.dtype != torch.bfloat16 or tuple(scales.shape) != (L, H, n_groups) or not scales.is_contiguous():
+        raise ValueError(f"scales must be contiguous bf16 {(L, H, n_groups)}")
+    if freqs.dtype != torch.float64 or freqs.dim() != 3 or tuple(freqs.shape[1:]) != (64, 2) \
+            or not freqs.is_contiguous():
+        raise ValueError("freqs must be contiguous float64 [max_pos, 64, 2]")
+    if positions.dtype != torch.int32 or tuple(positions.shape) != (L, 3) or not positions.is_contiguous():
+        raise ValueError(f"positions must be contiguous int32 {(L, 3)}")
+    if sink is not None and (sink.dtype != torch.bfloat16 or sink.shape[0] < min(sink_tokens, L)
+                             or tuple(sink.shape[1:]) != (H, D) or not sink.is_contiguous()):
+        raise ValueError("sink must be contiguous bf16 [>=sink_tokens, H, D]")
+    cb = _host_map(chan_band)
+    with torch.cuda.device(dev):
+        rc = _lib.load().kvq_rope_quantize(
+            _ptr(x), xs, _ptr(codes), _ptr(scales), _ptr(sink), int(sink_tokens) if sink is not None else 0,
+            L, H, D, cb.ctypes.data_as(ctypes.c_void_p), int(n_groups), int(bits), _ptr(freqs), freqs.shape[0],
+            _ptr(positions), _stream(dev))
+    _lib.check(rc, "kvq_rope_quantize")
+
+
 def quantize_layers_into(xs: list[torch.Tensor], codes: list[torch.Tensor], scales: list[torch.Tensor], chan_band,
                          n_groups: int, bits: int = 4, sinks: list[torch.Tensor | None] | None = None,
                          sink_tokens: int = 0) -> None:

@@ -181,6 +181,28 @@ class QuantKVTensor:
             v = v.to(self.device)
         _write_tensors([(self, v)], a, b)
 
+    def write_rope_(self, a, b, value, freqs, positions):
+        """Slice write [a, b) of keys before their rotary embedding, rotated in the
+        quantize kernel (kvq_rope_quantize): value [B, b-a, H, 128] bf16, freqs
+        [P, 64, 2] float64 on the cache's device (kvq.rope.freqs), positions
+        [b-a, 3] int32 (frame, height, width; kvq.rope.grid_positions), shared by
+        the streams. Equal to writing the rotated keys (quant_kv.py:201-215)."""
+        v = value.unsqueeze(0) if value.dim() == 3 else value
+        assert v.dim() == 4 and v.shape[0] == self.n_streams and v.shape[1] == b - a
+        v = v.to(device=self.device, dtype=self.dtype)
+        freqs = freqs.to(self.device).contiguous()
+        positions = positions.to(device=self.device, dtype=torch.int32).contiguous()
+        G = len(self.bands)
+        ns = max(0, min(b, self.sink_tokens) - a) if self.sink is not None else 0
+        for i in range(self.n_streams):
+            x = v[i]
+            if x.stride(2) != 1 or x.stride(1) != self.head_dim or x.data_ptr() % 16 or x.stride(0) % 8:
+                x = x.contiguous()
+            rows = self._rows(i, a, b)
+            sink = self.sink[self._sink_rows(i, a, a + ns)] if ns > 0 else None
+            _ops.rope_quantize_into(x, self.packed[rows], self.scales[rows], self.chan_band_host, G, self.bits,
+                                    freqs, positions, sink=sink, sink_tokens=ns)
+
     def read(self, a, b, out=None):
         """Dequantize tokens [a, b) with the sink overlay -> [B, b-a, H, D] bf16."""
         B, H, D = self.n_streams, self.n_heads, self.head_dim

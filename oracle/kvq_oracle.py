@@ -211,3 +211,31 @@ def attention_fp32(q_bits: np.ndarray, k_bits: np.ndarray, v_bits: np.ndarray,
             p /= p.sum(axis=-1, keepdims=True)
             out[b, :, h, :] = p @ v[b, :, h, :]
     return out
+
+
+# ----------------------------------------------------------------------------- rotary embedding
+ROPE_SPLIT = (22, 21, 21)  # complex pairs per axis (frame, height, width) for head_dim 128
+
+
+def rope_f64(x_bits: np.ndarray, freqs: np.ndarray, pos: np.ndarray) -> np.ndarray:
+    """Rotary embedding of bf16 keys [L, H, 128] as the upstream runtime applies it
+    before the cache write (Wan's rope_apply; not vendored in the reference, whose
+    band split is cited at quant_kv.py:26-31 and bench_qkv.py:64-65): pairs
+    (2i, 2i+1) as complex128 numbers times freqs[pos[t][axis(i)], i] = (cos, sin),
+    the product's real and imaginary parts rounded to float32 (the upstream
+    result) and then to bf16 (the cache dtype). freqs: [P, 64, 2] float64;
+    pos: [L, 3] int (frame, height, width); axis(i) = 0, 1, 2 for pairs
+    [0, 22), [22, 43), [43, 64). Separate IEEE fp64 products and sums."""
+    x = bf16_to_f32(x_bits).astype(np.float64)
+    L, H, D = x.shape
+    assert D == 128
+    x0, x1 = x[..., 0::2], x[..., 1::2]                      # [L, H, 64]
+    axis = np.repeat(np.arange(3), ROPE_SPLIT)               # [64]
+    p = np.clip(np.asarray(pos, dtype=np.int64), 0, freqs.shape[0] - 1)[:, axis]   # [L, 64]
+    cs = freqs[p, np.arange(64)[None, :]]                    # [L, 64, 2]
+    c, s = cs[..., 0][:, None, :], cs[..., 1][:, None, :]
+    y0 = x0 * c - x1 * s
+    y1 = x0 * s + x1 * c
+    y = np.empty_like(x)
+    y[..., 0::2], y[..., 1::2] = y0, y1
+    return f32_to_bf16(y.astype(np.float32))
