@@ -258,6 +258,12 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 template <class L, int KB, bool STATS>
 __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_constant__ Args a) {
   using GEO = Geo<KB>;
@@ -377,18 +383,22 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
       uint32_t s0[32], s1[32];
       tmem_ld32x2_wait(tS, tS + 32, s0, s1);
       const int valid = min(BN, a.Lk - j * BN);
-      float mx = -INFINITY;
+      // row max: 8 independent chains of three-input maxima
+      float pm[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) pm[i] = -INFINITY;
       if (valid == BN) {
 #pragma unroll
-        for (int c = 0; c < 32; ++c) mx = fmaxf(mx, fmaxf(__uint_as_float(s0[c]), __uint_as_float(s1[c])));
+        for (int c = 0; c < 32; ++c) pm[c & 7] = fmax3(pm[c & 7], __uint_as_float(s0[c]), __uint_as_float(s1[c]));
       } else {
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
-          if (c < valid) mx = fmaxf(mx, __uint_as_float(s0[c]));
-          if (32 + c < valid) mx = fmaxf(mx, __uint_as_float(s1[c]));
+          if (c < valid) pm[c & 7] = fmaxf(pm[c & 7], __uint_as_float(s0[c]));
+          if (32 + c < valid) pm[c & 7] = fmaxf(pm[c & 7], __uint_as_float(s1[c]));
         }
       }
-      const float mt = mx * a.scale_log2;
+      const float mt =
+          fmax3(fmax3(pm[0], pm[1], pm[2]), fmax3(pm[3], pm[4], pm[5]), fmaxf(pm[6], pm[7])) * a.scale_log2;
       bool rescale = false;
       float alpha = 1.0f;
       if (j == 0) {
@@ -429,24 +439,27 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
       const float nm = -m;
       float sum = 0.0f, sumb = 0.0f;
       uint32_t pw[32];
+      // P for tokens 0-31 of the tile (S columns 0-31) then 32-63: the first half's
+      // TMEM store runs while the second half is computed
+      auto half = [&](const uint32_t (&sv)[32], int base) {
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        const float x0 = fmaf(__uint_as_float(s0[2 * c]), a.scale_log2, nm);
-        const float x1 = fmaf(__uint_as_float(s0[2 * c + 1]), a.scale_log2, nm);
-        const float x2 = fmaf(__uint_as_float(s1[2 * c]), a.scale_log2, nm);
-        const float x3 = fmaf(__uint_as_float(s1[2 * c + 1]), a.scale_log2, nm);
-        float p0 = ex2(x0), p1 = ex2(x1), p2 = ex2(x2), p3 = ex2(x3);
-        if (valid < BN) {
-          p0 = (2 * c < valid) ? p0 : 0.0f;
-          p1 = (2 * c + 1 < valid) ? p1 : 0.0f;
-          p2 = (32 + 2 * c < valid) ? p2 : 0.0f;
-          p3 = (33 + 2 * c < valid) ? p3 : 0.0f;
+        for (int c = 0; c < 16; ++c) {
+          const float x0 = fmaf(__uint_as_float(sv[2 * c]), a.scale_log2, nm);
+          const float x1 = fmaf(__uint_as_float(sv[2 * c + 1]), a.scale_log2, nm);
+          float p0 = ex2(x0), p1 = ex2(x1);
+          if (valid < BN) {
+            p0 = (base + 2 * c < valid) ? p0 : 0.0f;
+            p1 = (base + 2 * c + 1 < valid) ? p1 : 0.0f;
+          }
+          sum += p0 + p1;
+          if (STATS) sumb += p0 * x0 + p1 * x1;
+          pw[base / 2 + c] = pack_bf16x2(p0, p1);
         }
-        sum += (p0 + p1) + (p2 + p3);
-        if (STATS) sumb += (p0 * x0 + p1 * x1) + (p2 * x2 + p3 * x3);
-        pw[c] = pack_bf16x2(p0, p1);
-        pw[16 + c] = pack_bf16x2(p2, p3);
-      }
+      };
+      half(s0, 0);
+      tmem_st16(tS, pw);
+      half(s1, 32);
+      tmem_st16(tS + 16, pw + 16);
       l += sum;
       if (STATS) {
         lb += sumb;
@@ -466,8 +479,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
           ls += part;
         }
       }
-      tmem_st32(tS, pw);  // P_x(j), 64 bf16 = 32 columns, over S_x(j)
-      tmem_wait_st();
+      tmem_wait_st();  // P_x(j), 64 bf16 = 32 columns, over S_x(j)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[bPFull + 2 * x + (j & 1)]);
