@@ -30,7 +30,8 @@
 
 namespace kvq {
 
-constexpr int kQT = 128;  // threads per CTA = rows per tile (fast quantize)
+constexpr int kQT = 128;  // threads per CTA = rows per tile (dequantize)
+constexpr int kQR = 128;  // threads per CTA = rows per tile (quantize)
 constexpr int kQD = 128;  // head_dim of the specialised kernels
 
 struct QuantArgs {
@@ -238,17 +239,15 @@ __device__ __forceinline__ void cp_async_wait() {
 
 template <int BITS>
 struct PipeCfg {
-  static constexpr int kStages = 2;  // keeps three CTAs per SM
+  static constexpr int kStages = 2;  // one tile in flight per CTA, three CTAs per SM (int4)
+  static constexpr int kMaxPerSm = 3;
 };
 
 template <class L, int BITS>
 constexpr int pipe_smem_bytes() {
-  return PipeCfg<BITS>::kStages * kQT * 256 + kQT * QuantConsts<BITS>::kCodeBytes + ((kQT * L::G * 2 + 15) / 16) * 16;
+  return PipeCfg<BITS>::kStages * kQR * 256 + kQR * QuantConsts<BITS>::kCodeBytes + ((kQR * L::G * 2 + 15) / 16) * 16;
 }
 
-// Persistent CTAs walk the 128-row tiles with a grid stride; each thread keeps
-// the next kStages-1 tiles' input in flight (cp.async, 16 bytes per copy, into
-// the XOR-swizzled layout) while it quantizes its row of the current tile.
 // Rotary embedding of one staged row in place (16 chunks of 4 bf16 pairs, XOR-
 // swizzled), as the upstream complex128 product (x0 + i x1)(cos + i sin) =
 // (x0 cos - x1 sin) + i (x0 sin + x1 cos), rounded to fp32 and then to bf16 (the
@@ -280,17 +279,20 @@ __device__ __forceinline__ void rope_row(const QuantArgs& a, int64_t token, uint
   }
 }
 
+// Persistent CTAs walk the kQR-row tiles with a grid stride; each thread keeps
+// the next kStages-1 tiles' input in flight (cp.async, 16 bytes per copy, into
+// the XOR-swizzled layout) while it quantizes its row of the current tile.
 template <class L, int BITS, class P, bool ROPE>
-__global__ void __launch_bounds__(kQT, 3) quantize_rows_pipe(const __grid_constant__ P bt, int64_t n_tiles) {
+__global__ void __launch_bounds__(kQR, 3) quantize_rows_pipe(const __grid_constant__ P bt, int64_t n_tiles) {
   using C = QuantConsts<BITS>;
   constexpr int G = L::G;
   constexpr int S = PipeCfg<BITS>::kStages;
   constexpr int CW = C::kCodeBytes;
   constexpr int CCH = CW / 16;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint4* sm_in = reinterpret_cast<uint4*>(smem_raw);                                   // S x kQT x 16 chunks
-  uint4* sm_codes = reinterpret_cast<uint4*>(smem_raw + S * kQT * 256);                // kQT x CCH
-  uint16_t* sm_sc = reinterpret_cast<uint16_t*>(smem_raw + S * kQT * 256 + kQT * CW);  // kQT x G
+  uint4* sm_in = reinterpret_cast<uint4*>(smem_raw);                                   // S x kQR x 16 chunks
+  uint4* sm_codes = reinterpret_cast<uint4*>(smem_raw + S * kQR * 256);                // kQR x CCH
+  uint16_t* sm_sc = reinterpret_cast<uint16_t*>(smem_raw + S * kQR * 256 + kQR * CW);  // kQR x G
   const int tid = threadIdx.x;
   const uint32_t in_base = static_cast<uint32_t>(__cvta_generic_to_shared(sm_in));
 
@@ -306,14 +308,14 @@ __global__ void __launch_bounds__(kQT, 3) quantize_rows_pipe(const __grid_consta
   };
   auto issue = [&](int64_t ti, int64_t loc, int stage) {
     const QuantArgs& a = bt.tensor(ti);
-    const int64_t row0 = loc * kQT;
-    const int nrows = static_cast<int>(min(static_cast<int64_t>(kQT), a.n_rows - row0));
+    const int64_t row0 = loc * kQR;
+    const int nrows = static_cast<int>(min(static_cast<int64_t>(kQR), a.n_rows - row0));
 #pragma unroll 4
-    for (int i = tid; i < kQT * 16; i += kQT) {
+    for (int i = tid; i < kQR * 16; i += kQR) {
       const int r = i >> 4, c = i & 15;
       if (r < nrows) {
         const uint16_t* src = x_row_ptr(a, row0 + r, kQD) + c * 8;
-        cp_async16(in_base + (((stage * kQT + r) * 16 + (c ^ (r & 7))) << 4), src);
+        cp_async16(in_base + (((stage * kQR + r) * 16 + (c ^ (r & 7))) << 4), src);
       }
     }
   };
@@ -340,15 +342,15 @@ __global__ void __launch_bounds__(kQT, 3) quantize_rows_pipe(const __grid_consta
     cp_async_wait<S - 1>();
     __syncthreads();
     const int stage = static_cast<int>(k % S);
-    const uint4* tin = sm_in + stage * kQT * 16;
+    const uint4* tin = sm_in + stage * kQR * 16;
     const QuantArgs& a = bt.tensor(ci);
-    const int64_t row0 = cl * kQT;
+    const int64_t row0 = cl * kQR;
     advance(ci, cl);
-    const int nrows = static_cast<int>(min(static_cast<int64_t>(kQT), a.n_rows - row0));
+    const int nrows = static_cast<int>(min(static_cast<int64_t>(kQR), a.n_rows - row0));
     if (tid < nrows) {
       // the rotated row replaces the staged input: the loads below, the exact-divide
       // fix-up and the sink copy all read the stage
-      if constexpr (ROPE) rope_row(a, (row0 + tid) / a.H, sm_in + stage * kQT * 16 + tid * 16, tid);
+      if constexpr (ROPE) rope_row(a, (row0 + tid) / a.H, sm_in + stage * kQR * 16 + tid * 16, tid);
       uint32_t w[64];
 #pragma unroll
       for (int c = 0; c < 16; ++c) {
@@ -380,7 +382,7 @@ __global__ void __launch_bounds__(kQT, 3) quantize_rows_pipe(const __grid_consta
     __syncthreads();
     {
       uint4* dst = reinterpret_cast<uint4*>(a.codes + row0 * CW);
-      for (int i = tid; i < nrows * CCH; i += kQT) {
+      for (int i = tid; i < nrows * CCH; i += kQR) {
         const int r = i / CCH, c = i % CCH;
         const int slot = (BITS == 4) ? (c ^ ((r >> 1) & 3)) : (c ^ (r & 7));
         st_global_v4(dst + i, sm_codes[r * CCH + slot]);
@@ -391,18 +393,18 @@ __global__ void __launch_bounds__(kQT, 3) quantize_rows_pipe(const __grid_consta
       const int n = nrows * G;
       if ((reinterpret_cast<uintptr_t>(dst) & 15) == 0 && (n % 8) == 0) {
         const uint4* s4 = reinterpret_cast<const uint4*>(sm_sc);
-        for (int i = tid; i < n / 8; i += kQT) st_global_v4(reinterpret_cast<uint4*>(dst) + i, s4[i]);
+        for (int i = tid; i < n / 8; i += kQR) st_global_v4(reinterpret_cast<uint4*>(dst) + i, s4[i]);
       } else if ((reinterpret_cast<uintptr_t>(dst) & 3) == 0 && (n % 2) == 0) {
         const uint32_t* s2 = reinterpret_cast<const uint32_t*>(sm_sc);
-        for (int i = tid; i < n / 2; i += kQT) reinterpret_cast<uint32_t*>(dst)[i] = s2[i];
+        for (int i = tid; i < n / 2; i += kQR) reinterpret_cast<uint32_t*>(dst)[i] = s2[i];
       } else {
-        for (int i = tid; i < n; i += kQT) dst[i] = sm_sc[i];
+        for (int i = tid; i < n; i += kQR) dst[i] = sm_sc[i];
       }
     }
     if (a.sink != nullptr && row0 < a.sink_rows) {
       const int ns = static_cast<int>(min(static_cast<int64_t>(nrows), a.sink_rows - row0));
       uint4* dst = reinterpret_cast<uint4*>(a.sink + row0 * kQD);
-      for (int i = tid; i < ns * 16; i += kQT) {
+      for (int i = tid; i < ns * 16; i += kQR) {
         const int r = i >> 4, c = i & 15;
         st_global_v4(dst + i, tin[r * 16 + (c ^ (r & 7))]);
       }
@@ -681,7 +683,8 @@ static int num_sms() {
 template <class L, int BITS, class P, bool ROPE = false>
 static int launch_fast(const P& b, int64_t tiles, cudaStream_t st) {
   constexpr int smem = pipe_smem_bytes<L, BITS>();
-  constexpr int per_sm = (227 * 1024) / smem < 3 ? (227 * 1024) / smem : 3;  // 3 for int4, 2 for int8
+  constexpr int cap_sm = PipeCfg<BITS>::kMaxPerSm;
+  constexpr int per_sm = (227 * 1024) / smem < cap_sm ? (227 * 1024) / smem : cap_sm;
   static_assert(per_sm >= 2, "at least two CTAs per SM must fit");
   // opt in to > 48 KB of dynamic shared memory once per device
   static bool configured[64];
@@ -698,7 +701,7 @@ static int launch_fast(const P& b, int64_t tiles, cudaStream_t st) {
   }
   const int64_t cap = static_cast<int64_t>(per_sm) * num_sms();
   const unsigned grid = static_cast<unsigned>(tiles < cap ? tiles : cap);
-  quantize_rows_pipe<L, BITS, P, ROPE><<<grid, kQT, smem, st>>>(b, tiles);
+  quantize_rows_pipe<L, BITS, P, ROPE><<<grid, kQR, smem, st>>>(b, tiles);
   return check_launch("kvq_quantize");
 }
 
@@ -780,7 +783,7 @@ static QuantArgs quant_args(const void* x, int64_t x_token_stride, void* codes, 
 static int quantize_tensors(int layout, const GroupMap& map, const QuantArgs* args, int n, int head_dim,
                             int n_groups, int bits, cudaStream_t st) {
   if (layout != kLayoutGeneric) {
-    const int64_t tpt = (args[0].n_rows + kQT - 1) / kQT;
+    const int64_t tpt = (args[0].n_rows + kQR - 1) / kQR;
     if (n == 1) {
       QuantOne o;
       o.a = args[0];
@@ -852,7 +855,7 @@ extern "C" int kvq_rope_quantize(const void* x, int64_t x_token_stride, void* co
   o.a.freqs = reinterpret_cast<const double2*>(freqs);
   o.a.pos = positions;
   o.a.max_pos = max_pos;
-  o.tiles_per = (o.a.n_rows + kQT - 1) / kQT;
+  o.tiles_per = (o.a.n_rows + kQR - 1) / kQR;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   return bits == 4 ? dispatch_fast<4, QuantOne, true>(layout, o, o.tiles_per, st)
                    : dispatch_fast<8, QuantOne, true>(layout, o, o.tiles_per, st);
