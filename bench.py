@@ -526,6 +526,28 @@ def run_extras(dev, peaks):
     del xs, cs, ss, xin
     torch.cuda.empty_cache()
 
+    # eviction in a window-21 cache (one layer's K and V): the 2 oldest frames after the
+    # sink leave, `kv[:, a:b] = kv[:, c:d].clone()` moves the rest down; the reference's
+    # dequantize + requantize (default) against the lossless packed move
+    L21 = 21 * FRAME
+    ev = {}
+    for lossless in (False, True):
+        kvs = [quant_kv.QuantKVTensor([1, L21, H_TOTAL, D], dev, torch.bfloat16, 4, MODE, SINK, lossless)
+               for _ in range(2)]
+        for i, c in enumerate(kvs):
+            c[:, 0:L21] = synth.make_k(L21, H_TOTAL, seed=80 + i, device=dev)
+        a0, c0 = SINK, SINK + 2 * FRAME
+        n = L21 - c0
+
+        def fe(_i):
+            for c in kvs:
+                c[:, a0:a0 + n] = c[:, c0:c0 + n].clone()
+        ms = _time_events(fe, 5)
+        ev["lossless" if lossless else "requantize"] = {"ms": statistics.median(ms), "tokens_moved": n}
+        del kvs
+        torch.cuda.empty_cache()
+    res["eviction_move_window21_layer_kv"] = ev
+
     # prefill (rebuild) per block, 40 layers: quantize the window's K and V into
     # the cache, then attention of the window's queries over the window; and the
     # 4 denoising steps' attention (4680 queries) over the same window

@@ -423,9 +423,10 @@ class PackedBlock(QuantKVWindow):
     def __init__(self, cache: QuantKVTensor, lo: int, hi: int):
         super().__init__(cache, lo, hi)
         L = hi - lo
-        self.packed = torch.cat([cache.packed[cache._rows(i, lo, hi)] for i in range(cache.n_streams)]).clone() \
+        # torch.cat allocates its result, so the snapshot is one copy of the rows
+        self.packed = torch.cat([cache.packed[cache._rows(i, lo, hi)] for i in range(cache.n_streams)]) \
             if L > 0 else cache.packed[:0].clone()
-        self.scales = torch.cat([cache.scales[cache._rows(i, lo, hi)] for i in range(cache.n_streams)]).clone() \
+        self.scales = torch.cat([cache.scales[cache._rows(i, lo, hi)] for i in range(cache.n_streams)]) \
             if L > 0 else cache.scales[:0].clone()
         self.n_exact = max(0, min(hi, cache.sink_tokens) - lo) if cache.sink is not None else 0
         self.exact = (torch.stack([cache.sink[cache._sink_rows(i, lo, lo + self.n_exact)]
