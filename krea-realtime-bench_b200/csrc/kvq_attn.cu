@@ -48,6 +48,7 @@
 #include <cuda_bf16.h>
 
 #include <cstring>
+#include <type_traits>
 #include <utility>
 
 #include "kvq_common.cuh"
@@ -282,9 +283,26 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
-  const int q0 = blockIdx.x * (2 * BM);
-  const int h = blockIdx.y;
-  const int b = blockIdx.z;
+  // One CTA per (pair of Q tiles, head, stream), 1-D grid. The CTAs with two Q
+  // tiles come first, pairs fastest (a head's packed K/V stays in L2 across its
+  // pairs); the last pairs that hold at most BM queries (one Q tile, about half
+  // the work) come after all of them, so that they fill the last wave instead of
+  // leaving a partial wave of full-length CTAs at the end.
+  const int n_pairs = (a.Lq + 2 * BM - 1) / (2 * BM);
+  const int n_full = a.Lq - (n_pairs - 1) * 2 * BM > BM ? n_pairs : n_pairs - 1;
+  const int n_hb = static_cast<int>(gridDim.x) / n_pairs;  // heads x streams
+  int pair, hb;
+  if (static_cast<int>(blockIdx.x) < n_full * n_hb) {
+    hb = static_cast<int>(blockIdx.x) / n_full;
+    pair = static_cast<int>(blockIdx.x) - hb * n_full;
+  } else {
+    hb = static_cast<int>(blockIdx.x) - n_full * n_hb;
+    pair = n_pairs - 1;
+  }
+  const int q0 = pair * (2 * BM);
+  const int h = hb % a.H;
+  const int b = hb / a.H;
+  const int nq = a.Lq - q0 > BM ? 2 : 1;  // Q tiles with queries
   const int nkv = (a.Lk + BN - 1) / BN;
 
   if (tid == 0) {
@@ -294,7 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
     }
     for (int i = 0; i < NS_KV; ++i) {
       mbar_init(&bars[bKvFull + i], 4);
-      mbar_init(&bars[bKvEmpty + i], 2);  // one arrival per Q tile (softmax warp 4x)
+      mbar_init(&bars[bKvEmpty + i], nq);  // one arrival per Q tile (softmax warp 4x)
     }
     for (int x = 0; x < 2; ++x) {
       mbar_init(&bars[bQReady + x], 4);
@@ -329,7 +347,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp < 8) {
+  if (warp < 4 * nq) {
     // ------------------------------------------------------------ softmax (Q tile x)
     const int x = warp >> 2;
     const int r = tid - x * BM;
@@ -371,32 +389,33 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
     // sink mass = ls / l, log-sum-exp = ln2 (m + log2 l).
     float lb = 0.0f, ls = 0.0f, mtrue = -INFINITY;
     bool ok = true;
-    for (int j = 0; j < nkv; ++j) {
+    // One KV tile. PART (the window's last tile when it holds fewer than BN
+    // tokens) is a separate instantiation: the column masking then costs nothing
+    // on the full tiles, where per-column selects would be issued every time.
+    auto step = [&](const int j, const int valid, auto part) -> bool {
+      constexpr bool PART = decltype(part)::value;
       const uint32_t tS = tS0 + 64 * (j & 1);
-      if (!mbar_wait_warp(&bars[bSFull + 2 * x + (j & 1)], (j >> 1) & 1, abort, &g_attn_status)) {
-        ok = false;
-        break;
-      }
+      if (!mbar_wait_warp(&bars[bSFull + 2 * x + (j & 1)], (j >> 1) & 1, abort, &g_attn_status)) return false;
       // S_x(j) complete => PV_x(j-2) complete: this Q tile no longer reads stage j-2
       if (j >= 2 && (warp & 3) == 0 && lane == 0) mbar_arrive(&bars[bKvEmpty + (j - 2) % NS_KV]);
       tc_fence_after();
       uint32_t s0[32], s1[32];
       tmem_ld32x2_wait(tS, tS + 32, s0, s1);
-      const int valid = min(BN, a.Lk - j * BN);
+      if constexpr (PART) {
+        // columns past the window: a finite logit so low that its weight is 0
+        // (finite, so that the entropy sum's p * t stays 0)
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          if (c >= valid) s0[c] = __float_as_uint(-1.0e30f);
+          if (32 + c >= valid) s1[c] = __float_as_uint(-1.0e30f);
+        }
+      }
       // row max: 8 independent chains of three-input maxima
       float pm[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) pm[i] = -INFINITY;
-      if (valid == BN) {
 #pragma unroll
-        for (int c = 0; c < 32; ++c) pm[c & 7] = fmax3(pm[c & 7], __uint_as_float(s0[c]), __uint_as_float(s1[c]));
-      } else {
-#pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          if (c < valid) pm[c & 7] = fmaxf(pm[c & 7], __uint_as_float(s0[c]));
-          if (32 + c < valid) pm[c & 7] = fmaxf(pm[c & 7], __uint_as_float(s1[c]));
-        }
-      }
+      for (int c = 0; c < 32; ++c) pm[c & 7] = fmax3(pm[c & 7], __uint_as_float(s0[c]), __uint_as_float(s1[c]));
       const float mt =
           fmax3(fmax3(pm[0], pm[1], pm[2]), fmax3(pm[3], pm[4], pm[5]), fmaxf(pm[6], pm[7])) * a.scale_log2;
       bool rescale = false;
@@ -421,10 +440,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
         // at the last tile, for the commit that follows PV_x(j-1).
         const bool last = j + 1 == nkv;
         if (!mbar_wait_warp(&bars[last ? bOReady + x : bSFull + 2 * x + ((j + 1) & 1)],
-                            last ? 0u : static_cast<uint32_t>(((j + 1) >> 1) & 1), abort, &g_attn_status)) {
-          ok = false;
-          break;
-        }
+                            last ? 0u : static_cast<uint32_t>(((j + 1) >> 1) & 1), abort, &g_attn_status))
+          return false;
         tc_fence_after();
 #pragma unroll 1
         for (int k = 0; k < 4; ++k) {
@@ -446,11 +463,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
         for (int c = 0; c < 16; ++c) {
           const float x0 = fmaf(__uint_as_float(sv[2 * c]), a.scale_log2, nm);
           const float x1 = fmaf(__uint_as_float(sv[2 * c + 1]), a.scale_log2, nm);
-          float p0 = ex2(x0), p1 = ex2(x1);
-          if (valid < BN) {
-            p0 = (base + 2 * c < valid) ? p0 : 0.0f;
-            p1 = (base + 2 * c + 1 < valid) ? p1 : 0.0f;
-          }
+          const float p0 = ex2(x0), p1 = ex2(x1);
           sum += p0 + p1;
           if (STATS) sumb += p0 * x0 + p1 * x1;
           pw[base / 2 + c] = pack_bf16x2(p0, p1);
@@ -483,6 +496,14 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[bPFull + 2 * x + (j & 1)]);
+      return true;
+    };
+    for (int j = 0; j < nkv; ++j) {
+      const int valid = min(BN, a.Lk - j * BN);
+      if (!(valid == BN ? step(j, valid, std::false_type{}) : step(j, valid, std::true_type{}))) {
+        ok = false;
+        break;
+      }
     }
     if (ok && mbar_wait_warp(&bars[bOFinal + x], 0, abort, &g_attn_status)) {
       tc_fence_after();
@@ -558,6 +579,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
       // consumer orders them by the kernel's completion (stream synchronize on
       // the writing rank, then a cross-rank barrier).
     }
+  } else if (warp < 8) {
+    // a Q tile without queries: nothing to do
   } else if (warp < kProdWarp) {
     // ------------------------------------------------------------ converters
     const int t = tid - kConvWarp0 * 32;
@@ -647,7 +670,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
   } else if (warp == kMmaWarp || warp == kMmaWarp + 1) {
     // ------------------------------------------------------------ MMA issuers
     const int x = warp - kMmaWarp;
-    if (lane == 0) {
+    if (lane == 0 && x < nq) {
       constexpr uint32_t idS = idesc_bf16(BM, BN, 0);
       constexpr uint32_t idPV = idesc_bf16(BM, D, 1);
       const uint32_t tS0 = tmem + kColS + 128 * x, tO = tmem + kColO + 128 * x;
@@ -777,8 +800,7 @@ int launch(const Args& a, int n_ctas, int batch, cudaStream_t st) {
     }
     configured[dev] = true;
   }
-  dim3 grid(n_ctas, a.H, batch);
-  attention_kernel<L, KB, STATS><<<grid, kThreads, kSmemBytes, st>>>(a);
+  attention_kernel<L, KB, STATS><<<n_ctas * a.H * batch, kThreads, kSmemBytes, st>>>(a);
   return check_launch("kvq_attention");
 }
 
@@ -810,6 +832,8 @@ static int attention_impl(const void* q, int64_t q_token_stride, const void* k_c
               "window [%lld, %lld) is empty or outside the cache of %lld tokens", (long long)lo, (long long)hi,
               (long long)cache_tokens);
   KVQ_REQUIRE(n_q <= (int64_t)1 << 30, KVQ_ERR_ARG, "too many queries");
+  KVQ_REQUIRE((n_q + 2 * attn::BM - 1) / (2 * attn::BM) * n_heads * batch <= 0x7FFFFFFF, KVQ_ERR_ARG,
+              "too many queries x heads x streams for one launch");
   KVQ_REQUIRE((int64_t)batch * cache_tokens < ((int64_t)1 << 31) - 256, KVQ_ERR_ARG,
               "batch * cache_tokens must stay below 2^31");
   KVQ_REQUIRE(sink_tokens >= 0 && sink_tokens <= cache_tokens, KVQ_ERR_ARG, "bad sink_tokens");

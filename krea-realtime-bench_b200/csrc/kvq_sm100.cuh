@@ -40,6 +40,22 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// The same with a suspend-time hint: a thread whose phase is not complete sleeps
+// until it completes or about kSuspendNs pass, instead of the shorter default,
+// so a long wait re-polls (and takes issue slots from the working warps of its
+// sub-partition) a few times instead of hundreds.
+constexpr uint32_t kSuspendNs = 0x989680u;  // 10 ms
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(kSuspendNs)
+      : "memory");
+  return ok != 0;
+}
 
 // Waits until the phase with the given parity of `bar` has completed. Gives up
 // after about a second, or at once when another thread already gave up
@@ -50,9 +66,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   if (mbar_try_wait(b, parity)) return true;
   const long long t0 = clock64();
   while (true) {
-#pragma unroll 1
-    for (int i = 0; i < 32; ++i)
-      if (mbar_try_wait(b, parity)) return true;
+    if (mbar_try_wait_sleep(b, parity)) return true;
     if (*abort) return false;
     if (clock64() - t0 > kWaitCycles) {
       *abort = 1;
