@@ -138,7 +138,7 @@ __device__ __forceinline__ void quant_group(const uint32_t (&w)[64], uint32_t (&
   {
     uint32_t lo = m << 16, hi = m & 0xFFFF0000u;
     float a = __uint_as_float(lo), b = __uint_as_float(hi);
-    amax = (a != a || b != b) ? __uint_as_float(0x7FC00000u) : fmaxf(a, b);
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(amax) : "f"(a), "f"(b));  // NaN if either is NaN
   }
   float s = group_scale<C::kQmax>(amax);
   s = (s > 0.0f) ? s : 1.0f;  // quant_kv.py:152 (also maps NaN to 1, like torch.where)
@@ -306,16 +306,34 @@ __global__ void __launch_bounds__(kQR, 3) quantize_rows_pipe(const __grid_consta
       ++ti;
     }
   };
+  // Thread t copies the 16-byte chunks t + kQR k of the tile: chunk t % 16 of rows
+  // t / 16 + 8 k. Its shared-memory destinations are 2048 bytes apart (the swizzle
+  // depends on the row mod 8 only), and so are its sources when the tile's rows are
+  // one contiguous range; strided rows step (token, head) by 8 heads per copy. The
+  // addresses come from one base per tile: per-copy 64-bit address arithmetic here
+  // cost more issue slots than the quantization itself.
   auto issue = [&](int64_t ti, int64_t loc, int stage) {
     const QuantArgs& a = bt.tensor(ti);
     const int64_t row0 = loc * kQR;
     const int nrows = static_cast<int>(min(static_cast<int64_t>(kQR), a.n_rows - row0));
+    const int r0 = tid >> 4, c = tid & 15;
+    const uint32_t dst = in_base + (((stage * kQR + r0) * 16 + (c ^ (r0 & 7))) << 4);
+    if (a.rows_contig && nrows == kQR) {
+      const char* src = reinterpret_cast<const char*>(a.x + row0 * kQD) + tid * 16;
+#pragma unroll
+      for (int k = 0; k < 16; ++k) cp_async16(dst + k * 2048, src + k * 2048);
+    } else {
+      int64_t t = (row0 + r0) / a.H;
+      int h = static_cast<int>(row0 + r0 - t * a.H);
 #pragma unroll 4
-    for (int i = tid; i < kQR * 16; i += kQR) {
-      const int r = i >> 4, c = i & 15;
-      if (r < nrows) {
-        const uint16_t* src = x_row_ptr(a, row0 + r, kQD) + c * 8;
-        cp_async16(in_base + (((stage * kQR + r) * 16 + (c ^ (r & 7))) << 4), src);
+      for (int k = 0; k < 16; ++k) {
+        if (r0 + 8 * k < nrows)
+          cp_async16(dst + k * 2048, a.x + t * a.x_token_stride + static_cast<int64_t>(h) * kQD + c * 8);
+        h += 8;
+        while (h >= a.H) {
+          h -= a.H;
+          ++t;
+        }
       }
     }
   };
@@ -646,7 +664,14 @@ __global__ void __launch_bounds__(kQT, 3) dequantize_rows_pipe(DequantArgs a, in
       deq_row_to<L>(orow, tid, w, sp, std::make_integer_sequence<int, 16>{});
     }
     __syncthreads();
-    if (a.rows_contig) {
+    if (a.rows_contig && nrows == kQT) {
+      // full tile, one contiguous range: thread t stores chunks t + kQT k (row
+      // t / 16 + 8 k, chunk t % 16), constant strides on both sides
+      uint4* dst = reinterpret_cast<uint4*>(a.out + row0 * kQD) + tid;
+      const uint4* src = sm_out + (tid >> 4) * 16 + ((tid & 15) ^ ((tid >> 4) & 7));
+#pragma unroll
+      for (int k = 0; k < 16; ++k) st_global_v4(dst + k * kQT, src[k * kQT]);
+    } else if (a.rows_contig) {
       uint4* dst = reinterpret_cast<uint4*>(a.out + row0 * kQD);
       for (int i = tid; i < nrows * 16; i += kQT) {
         const int r = i >> 4, c = i & 15;
