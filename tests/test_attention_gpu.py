@@ -1,7 +1,7 @@
 """Fused int4-KV attention against the oracle: the reference's window read
 (dequantize + bf16 sink overlay, quant_kv.py:189-199) followed by softmax
-attention in fp32. Tolerance: max-abs <= 2e-2 and
-mean-abs <= 2e-3 of the fp32 result, per call."""
+attention in fp32. Tolerance: max-abs <= 2e-2 and mean-abs <= 2e-3 of the
+fp32 result, per call."""
 import math
 
 import numpy as np
