@@ -19,9 +19,12 @@
 //                    the K rows and 10-11 the V rows (one row per thread) from
 //                    the TMA-staged codes into 128B-swizzled bf16 tiles, with
 //                    packed bf16x2 arithmetic (bit-identical to the reference).
-//   warp 12          TMA producer: packed codes (SWIZZLE_64B staging) and, for
-//                    tiles that reach into the sink, the bf16 sink rows straight
-//                    into the bf16 tiles (SWIZZLE_128B, the MMA's layout).
+//                    A row's scales of the next tile are loaded while the
+//                    current tile is converted.
+//   warps 12 / 15    TMA producers for K / V: packed codes (SWIZZLE_64B staging)
+//                    and, for tiles that reach into the sink, the bf16 sink rows
+//                    straight into the bf16 tiles (SWIZZLE_128B, the MMA's
+//                    layout).
 //   warps 13 / 14    one thread each issuing the tcgen05.mma of Q tile 0 / 1:
 //                    S_x = Q_x K^T (M=128, N=64, K=128, Q and K in shared
 //                    memory) and O_x += P_x V (M=128, N=128, K=64, P in TMEM, V
@@ -37,9 +40,13 @@
 //    every ~60-100 cycles and blocks ~250 cycles on each tcgen05.commit, which
 //    leaves the tensor pipe half idle; two threads keep it fed.
 //  - One commit per KV tile and thread (S_x full). Everything else is derived
-//    from it: the softmax that sees S_x(j) (issued behind PV_x(j-2)) releases
-//    K/V stage j-2; a rescale of O at tile j waits for S_x(j+1) (issued behind
-//    PV_x(j-1)).
+//    from it: the softmax that sees S_x(j) releases K stage j (read by S_x(j)
+//    only) and V stage j-2 (S_x(j) was issued behind PV_x(j-2)); a rescale of O
+//    at tile j waits for S_x(j+1) (issued behind PV_x(j-1)).
+//  - K and V run as two streams (own code stages, bf16 stages, barriers and
+//    producer): K stages come free two KV tiles before V stages, so the K rows
+//    of tile j+2 are converted well before S_x(j+2) is issued and their
+//    conversion is off the per-tile chain P_x(j) -> PV_x(j) -> S_x(j+2).
 // TMEM columns: O_0 [0,128) O_1 [128,256), S_0 [256,320) [320,384), S_1
 // [384,448) [448,512) (P over the first 32 columns of its S buffer).
 // Synchronisation is by mbarriers with one arrival per warp; every wait gives up
@@ -67,6 +74,7 @@ constexpr int D = 128;
 constexpr int NS_KV = 4;  // bf16 K/V tile stages
 constexpr int kThreads = 16 * 32;
 constexpr int kConvWarp0 = 8, kProdWarp = 12, kMmaWarp = 13;  // MMA issuers: warps 13 (Q tile 0), 14 (Q tile 1)
+constexpr int kProdWarpV = 15;                                  // warp 12 produces K, warp 15 V
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColO = 0, kColS = 256;  // S_x buffer u at kColS + 128x + 64u
 
@@ -91,8 +99,9 @@ struct Geo {
   static constexpr int kOffQ = kOffVC + NS_LD * kCodeTileV;
   static constexpr int kOffBar = kOffQ + 2 * kQTile;
   // barrier indices (S/P full: 2x + buffer)
-  static constexpr int bLdFull = 0, bLdEmpty = bLdFull + NS_LD, bKvFull = bLdEmpty + NS_LD,
-                       bKvEmpty = bKvFull + NS_KV, bQReady = bKvEmpty + NS_KV, bSFull = bQReady + 2,
+  // code stages and bf16 stages per tensor: index + NS_LD (NS_KV) for V
+  static constexpr int bLdFull = 0, bLdEmpty = bLdFull + 2 * NS_LD, bKvFull = bLdEmpty + 2 * NS_LD,
+                       bKvEmpty = bKvFull + 2 * NS_KV, bQReady = bKvEmpty + 2 * NS_KV, bSFull = bQReady + 2,
                        bPFull = bSFull + 4, bOReady = bPFull + 4, bOFinal = bOReady + 2, bMmaDone = bOFinal + 2,
                        bEpi = bMmaDone + 2, kNumBars = bEpi + 2;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
@@ -306,12 +315,12 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
   const int nkv = (a.Lk + BN - 1) / BN;
 
   if (tid == 0) {
-    for (int i = 0; i < NS_LD; ++i) {
+    for (int i = 0; i < 2 * NS_LD; ++i) {
       mbar_init(&bars[bLdFull + i], 1);
-      mbar_init(&bars[bLdEmpty + i], 4);
+      mbar_init(&bars[bLdEmpty + i], 2);  // the tensor's two converter warps
     }
-    for (int i = 0; i < NS_KV; ++i) {
-      mbar_init(&bars[bKvFull + i], 4);
+    for (int i = 0; i < 2 * NS_KV; ++i) {
+      mbar_init(&bars[bKvFull + i], 2);
       mbar_init(&bars[bKvEmpty + i], nq);  // one arrival per Q tile (softmax warp 4x)
     }
     for (int x = 0; x < 2; ++x) {
@@ -334,13 +343,10 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
     tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
   }
-  if (warp == kProdWarp && lane == 0) {
-    prefetch_tmap(&a.tm_kc);
-    prefetch_tmap(&a.tm_vc);
-    if (a.sink_tokens > 0) {
-      prefetch_tmap(&a.tm_ks);
-      prefetch_tmap(&a.tm_vs);
-    }
+  if ((warp == kProdWarp || warp == kProdWarpV) && lane == 0) {
+    const bool pv = warp != kProdWarp;
+    prefetch_tmap(pv ? &a.tm_vc : &a.tm_kc);
+    if (a.sink_tokens > 0) prefetch_tmap(pv ? &a.tm_vs : &a.tm_ks);
   }
   tc_fence_before();
   __syncthreads();
@@ -396,8 +402,12 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
       constexpr bool PART = decltype(part)::value;
       const uint32_t tS = tS0 + 64 * (j & 1);
       if (!mbar_wait_warp(&bars[bSFull + 2 * x + (j & 1)], (j >> 1) & 1, abort, &g_attn_status)) return false;
-      // S_x(j) complete => PV_x(j-2) complete: this Q tile no longer reads stage j-2
-      if (j >= 2 && (warp & 3) == 0 && lane == 0) mbar_arrive(&bars[bKvEmpty + (j - 2) % NS_KV]);
+      // S_x(j) complete => this Q tile no longer reads K stage j, and PV_x(j-2)
+      // (issued before it) is complete: nor V stage j-2
+      if ((warp & 3) == 0 && lane == 0) {
+        mbar_arrive(&bars[bKvEmpty + j % NS_KV]);
+        if (j >= 2) mbar_arrive(&bars[bKvEmpty + NS_KV + (j - 2) % NS_KV]);
+      }
       tc_fence_after();
       uint32_t s0[32], s1[32];
       tmem_ld32x2_wait(tS, tS + 32, s0, s1);
@@ -589,16 +599,27 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
     const uint16_t* scales = is_v ? a.vs : a.ks;
     const uint32_t codes_base = sbase + (is_v ? kOffVC : kOffKC);
     const uint32_t kv_base = sbase + (is_v ? kOffV : kOffK);
+    // this row's scales of tile j + 1 are loaded while tile j is converted
+    auto load_sw = [&](int jj, ScaleWords<L>& sw) {
+      const int jt = jj * BN + r;
+      const int64_t tok = a.lo + jt;
+      if (jj < nkv && jt < a.Lk && tok >= a.sink_tokens)
+        load_scale_words<L>(scales + ((static_cast<int64_t>(b) * a.cache_tokens + tok) * a.H + h) * L::G, sw);
+    };
+    ScaleWords<L> sw_next;
+    load_sw(0, sw_next);
     for (int j = 0; j < nkv; ++j) {
       const int ls = j % NS_LD, ks = j % NS_KV;
       const int jt = j * BN + r;
       const int64_t tok = a.lo + jt;
       const bool live = jt < a.Lk;
       const bool coded = live && tok >= a.sink_tokens;
-      ScaleWords<L> sw;
-      if (coded) load_scale_words<L>(scales + ((static_cast<int64_t>(b) * a.cache_tokens + tok) * a.H + h) * L::G, sw);
-      if (!mbar_wait_warp(&bars[bLdFull + ls], (j / NS_LD) & 1, abort, &g_attn_status)) break;
-      if (j >= NS_KV && !mbar_wait_warp(&bars[bKvEmpty + ks], ((j / NS_KV) - 1) & 1, abort, &g_attn_status)) break;
+      const ScaleWords<L> sw = sw_next;
+      load_sw(j + 1, sw_next);
+      if (!mbar_wait_warp(&bars[bLdFull + is_v * NS_LD + ls], (j / NS_LD) & 1, abort, &g_attn_status)) break;
+      if (j >= NS_KV &&
+          !mbar_wait_warp(&bars[bKvEmpty + is_v * NS_KV + ks], ((j / NS_KV) - 1) & 1, abort, &g_attn_status))
+        break;
       const uint32_t dst = kv_base + ks * kKVTile;
       if (!live) {
 #pragma unroll
@@ -630,39 +651,44 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive(&bars[bLdEmpty + ls]);
-        mbar_arrive(&bars[bKvFull + ks]);
+        mbar_arrive(&bars[bLdEmpty + is_v * NS_LD + ls]);
+        mbar_arrive(&bars[bKvFull + is_v * NS_KV + ks]);
       }
     }
-  } else if (warp == kProdWarp) {
-    // ------------------------------------------------------------ TMA producer
+  } else if (warp == kProdWarp || warp == kProdWarpV) {
+    // ------------------------------------------------------------ TMA producers
+    // warp 12: K codes and K sink rows; warp 15: V
+    const int pv = warp != kProdWarp;
     if (lane == 0) {
+      const CUtensorMap* tc = pv ? &a.tm_vc : &a.tm_kc;
+      const CUtensorMap* tsk = pv ? &a.tm_vs : &a.tm_ks;
+      const uint32_t code_tile = pv ? static_cast<uint32_t>(kCodeTileV) : static_cast<uint32_t>(kCodeTileK);
+      const uint32_t code_base = sbase + (pv ? kOffVC : kOffKC);
+      const uint32_t kv_base = sbase + (pv ? kOffV : kOffK);
+      const int code_x = h * (pv ? 64 : (KB == 4 ? 64 : 128));
       for (int j = 0; j < nkv; ++j) {
         const int ls = j % NS_LD, ks = j % NS_KV;
-        if (j >= NS_LD && !mbar_wait(&bars[bLdEmpty + ls], ((j / NS_LD) - 1) & 1, abort, &g_attn_status)) break;
+        if (j >= NS_LD && !mbar_wait(&bars[bLdEmpty + pv * NS_LD + ls], ((j / NS_LD) - 1) & 1, abort, &g_attn_status))
+          break;
         const int64_t t0 = a.lo + static_cast<int64_t>(j) * BN;
         const int64_t t1 = a.lo + min(static_cast<int64_t>(j + 1) * BN, static_cast<int64_t>(a.Lk));
         const bool has_sink = t0 < a.sink_tokens;
         const bool has_codes = t1 > a.sink_tokens;
         if (has_sink && j >= NS_KV &&
-            !mbar_wait(&bars[bKvEmpty + ks], ((j / NS_KV) - 1) & 1, abort, &g_attn_status))
+            !mbar_wait(&bars[bKvEmpty + pv * NS_KV + ks], ((j / NS_KV) - 1) & 1, abort, &g_attn_status))
           break;
-        const uint32_t bytes = (has_codes ? static_cast<uint32_t>(kCodeTileK + kCodeTileV) : 0u) +
-                               (has_sink ? 2u * kKVTile : 0u);
-        mbar_arrive_expect_tx(&bars[bLdFull + ls], bytes);
+        const uint32_t bytes = (has_codes ? code_tile : 0u) + (has_sink ? static_cast<uint32_t>(kKVTile) : 0u);
+        uint64_t* full = &bars[bLdFull + pv * NS_LD + ls];
+        mbar_arrive_expect_tx(full, bytes);
         if (has_codes) {
           const int row = static_cast<int>(static_cast<int64_t>(b) * a.cache_tokens + t0);
-          tma_load_2d(sbase + kOffKC + ls * kCodeTileK, &a.tm_kc, h * (KB == 4 ? 64 : 128), row,
-                      &bars[bLdFull + ls]);
-          tma_load_2d(sbase + kOffVC + ls * kCodeTileV, &a.tm_vc, h * 64, row, &bars[bLdFull + ls]);
+          tma_load_2d(code_base + ls * code_tile, tc, code_x, row, full);
         }
         if (has_sink) {
           const int row = static_cast<int>(static_cast<int64_t>(b) * a.sink_tokens + t0);
-          const uint32_t kd = sbase + kOffK + ks * kKVTile, vd = sbase + kOffV + ks * kKVTile;
-          tma_load_2d(kd, &a.tm_ks, h * D, row, &bars[bLdFull + ls]);
-          tma_load_2d(kd + kAtom, &a.tm_ks, h * D + 64, row, &bars[bLdFull + ls]);
-          tma_load_2d(vd, &a.tm_vs, h * D, row, &bars[bLdFull + ls]);
-          tma_load_2d(vd + kAtom, &a.tm_vs, h * D + 64, row, &bars[bLdFull + ls]);
+          const uint32_t d = kv_base + ks * kKVTile;
+          tma_load_2d(d, tsk, h * D, row, full);
+          tma_load_2d(d + kAtom, tsk, h * D + 64, row, full);
         }
       }
     }
@@ -707,6 +733,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
       }
       for (int j = 0; j < nkv && ok; ++j) {
         if (!(ok = mbar_wait(&bars[bPFull + 2 * x + (j & 1)], (j >> 1) & 1, abort, &g_attn_status))) break;
+        if (!(ok = mbar_wait(&bars[bKvFull + NS_KV + j % NS_KV], (j / NS_KV) & 1, abort, &g_attn_status))) break;
         tc_fence_after();
         issue_pv(j);
         if (j + 2 < nkv) {
