@@ -732,14 +732,16 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
         }
       }
       for (int j = 0; j < nkv && ok; ++j) {
-        if (!(ok = mbar_wait(&bars[bPFull + 2 * x + (j & 1)], (j >> 1) & 1, abort, &g_attn_status))) break;
+        // V(j) and K(j+2) were converted tiles ago (their stages came free at
+        // S(j-2)): confirm them before waiting for P_x(j), off the chain
+        // P_x(j) -> PV_x(j) -> S_x(j+2)
         if (!(ok = mbar_wait(&bars[bKvFull + NS_KV + j % NS_KV], (j / NS_KV) & 1, abort, &g_attn_status))) break;
+        if (j + 2 < nkv && !(ok = wait_kv(j + 2))) break;
+        if (!(ok = mbar_wait(&bars[bPFull + 2 * x + (j & 1)], (j >> 1) & 1, abort, &g_attn_status))) break;
         tc_fence_after();
         issue_pv(j);
         if (j + 2 < nkv) {
           // S_x(j+2) into the buffer PV_x(j) is reading: behind it in issue order
-          if (!(ok = wait_kv(j + 2))) break;
-          tc_fence_after();
           issue_s(j + 2);
         } else if (j + 2 == nkv) {
           mma_commit(&bars[bOReady + x]);  // PV_x(nkv-2): a rescale at the last tile waits for it
