@@ -14,7 +14,10 @@
 //                    128B-swizzled K-major layout); per KV tile reads S (64
 //                    columns) from TMEM, online base-2 softmax with lazy
 //                    rescaling of O (only when the row max grows by > 2^8),
-//                    writes P as bf16 back into TMEM over S; finally normalises O.
+//                    writes P as bf16 back into TMEM over S; finally normalises O
+//                    and stores it: staged in the Q buffer and written by two TMA
+//                    tensor stores per destination (kvq_attention, the gather), or
+//                    with per-thread stores (kvq_attention_stats).
 //   warps 8-11       converters: per KV tile of 64 tokens, warps 8-9 dequantize
 //                    the K rows and 10-11 the V rows (one row per thread) from
 //                    the TMA-staged codes into 128B-swizzled bf16 tiles, with
