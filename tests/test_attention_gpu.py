@@ -130,6 +130,28 @@ def test_custom_scale_and_out_buffer():
     _check(o, ref, "scale 0.05")
 
 
+def test_padded_q_and_out_views():
+    """q and out as views into wider buffers (a padding head on each side, so the
+    token stride is (H + 2) * 128): the output tile is stored by TMA through a map
+    that covers the H real heads and Lq rows of each stream, so the padding heads
+    keep their contents and no stream's partial last tile spills into the next."""
+    import quant_kv
+    from kvq import synth
+    B, S, H, Lq, sink = 2, 300, 3, 200, 64
+    tk, tv, kb, vb = _make_caches(B, S, H, "bands4", sink, seed=11)
+    q = synth.make_q(B, Lq, H, seed=12)
+    qbuf = torch.zeros((B, Lq, H + 2, 128), dtype=torch.bfloat16, device="cuda")
+    qbuf[:, :, 1:H + 1] = q.cuda()
+    obuf = torch.full((B, Lq, H + 2, 128), 7.0, dtype=torch.bfloat16, device="cuda")
+    o = quant_kv.attention(qbuf[:, :, 1:H + 1], tk[:, 0:S], tv[:, 0:S], out=obuf[:, :, 1:H + 1])
+    assert o.data_ptr() == obuf[:, :, 1:H + 1].data_ptr()
+    bands = ko.band_edges(128, "bands4")
+    kw = np.stack([_oracle_window(kb[b], bands, sink, 0, S) for b in range(B)])
+    vw = np.stack([_oracle_window(vb[b], bands, sink, 0, S) for b in range(B)])
+    _check(obuf[:, :, 1:H + 1], _oracle_attention(_u16(q), kw, vw), "padded q and out")
+    assert torch.all(obuf[:, :, 0] == 7.0) and torch.all(obuf[:, :, H + 1] == 7.0), "padding heads written"
+
+
 def test_plain_tensors_are_rejected_and_status_is_clean():
     import quant_kv
     from kvq import ops
