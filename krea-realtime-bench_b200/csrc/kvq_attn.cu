@@ -10,8 +10,7 @@
 // One CTA per (pair of 128-row Q tiles, head, stream); the two Q tiles share
 // every dequantized K/V tile. 512 threads, warp-specialised:
 //   warps 0-3 / 4-7  softmax for Q tile 0 / 1: thread r owns Q row r (TMEM lane
-//                    r). Stores its Q row into shared memory once (the MMA's
-//                    128B-swizzled K-major layout); per KV tile reads S (64
+//                    r). Per KV tile reads S (64
 //                    columns) from TMEM, online base-2 softmax with lazy
 //                    rescaling of O (only when the row max grows by > 2^8),
 //                    writes P as bf16 back into TMEM over S; finally normalises O
@@ -27,7 +26,9 @@
 //   warps 12 / 15    TMA producers for K / V: packed codes (SWIZZLE_64B staging)
 //                    and, for tiles that reach into the sink, the bf16 sink rows
 //                    straight into the bf16 tiles (SWIZZLE_128B, the MMA's
-//                    layout).
+//                    layout). Warp 12 first loads the Q tiles by TMA (the S
+//                    MMA's 128B-swizzled K-major layout; rows past n_q read 0):
+//                    per-thread Q loads had made each CTA's start ~2.5x slower.
 //   warps 13 / 14    one thread each issuing the tcgen05.mma of Q tile 0 / 1:
 //                    S_x = Q_x K^T (M=128, N=64, K=128, Q and K in shared
 //                    memory) and O_x += P_x V (M=128, N=128, K=64, P in TMEM, V
@@ -118,6 +119,7 @@ constexpr int kMaxOut = 8;
 struct alignas(64) Args {
   CUtensorMap tm_kc, tm_vc;  // codes [B*S rows, H*64 B (int8 K: H*128 B)], box 64 (128) x 64, SWIZZLE_64B (128B)
   CUtensorMap tm_ks, tm_vs;  // sinks [B*sink rows, H*128 bf16], box 64 x 64, SWIZZLE_128B
+  CUtensorMap tm_q;          // q as [batch][n_q][H * D] bf16, box 64 x 128 x 1, SWIZZLE_128B (rows past n_q read 0)
   const uint16_t* q;
   int64_t q_tok_stride, q_batch_stride;
   const uint16_t* ks;
@@ -327,7 +329,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
       mbar_init(&bars[bKvEmpty + i], nq);  // one arrival per Q tile (softmax warp 4x)
     }
     for (int x = 0; x < 2; ++x) {
-      mbar_init(&bars[bQReady + x], 4);
+      mbar_init(&bars[bQReady + x], 1);  // the K producer's expect_tx; Q arrives by TMA
       mbar_init(&bars[bSFull + 2 * x], 1);
       mbar_init(&bars[bSFull + 2 * x + 1], 1);
       mbar_init(&bars[bPFull + 2 * x], 4);
@@ -348,6 +350,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
   }
   if ((warp == kProdWarp || warp == kProdWarpV) && lane == 0) {
     const bool pv = warp != kProdWarp;
+    if (!pv) prefetch_tmap(&a.tm_q);
     prefetch_tmap(pv ? &a.tm_vc : &a.tm_kc);
     if (a.sink_tokens > 0) prefetch_tmap(pv ? &a.tm_vs : &a.tm_ks);
   }
@@ -364,33 +367,6 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
     const uint32_t tO = tmem + lane_off + kColO + 128 * x;
     const uint32_t tS0 = tmem + lane_off + kColS + 128 * x;
     const int qi = q0 + x * BM + r;
-    {
-      uint32_t qw[64];
-      if (qi < a.Lq) {
-        const uint16_t* src = a.q + b * a.q_batch_stride + static_cast<int64_t>(qi) * a.q_tok_stride +
-                              static_cast<int64_t>(h) * D;
-#pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          uint4 v = ld_global_nc_v4(src + 8 * c);
-          qw[4 * c] = v.x;
-          qw[4 * c + 1] = v.y;
-          qw[4 * c + 2] = v.z;
-          qw[4 * c + 3] = v.w;
-        }
-      } else {
-#pragma unroll
-        for (int c = 0; c < 64; ++c) qw[c] = 0u;
-      }
-      // row r of Q_x in the K-major SWIZZLE_128B layout of the S MMA's A operand
-      const uint32_t qdst = sbase + kOffQ + x * kQTile + r * 128;
-#pragma unroll
-      for (int c = 0; c < 16; ++c)
-        st_shared_v4(qdst + (c >> 3) * kQAtom + (((c & 7) ^ (r & 7)) << 4),
-                     make_uint4(qw[4 * c], qw[4 * c + 1], qw[4 * c + 2], qw[4 * c + 3]));
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars[bQReady + x]);
-    }
     float m = -INFINITY, l = 0.0f;
     // STATS: with e = 2^(t - m) (t = scaled logit in log2 units), lb = sum e (t - m),
     // ls = sum of e over sink tokens, mtrue = the row's true max of t (m may lag it
@@ -662,6 +638,15 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
     // ------------------------------------------------------------ TMA producers
     // warp 12: K codes and K sink rows; warp 15: V
     const int pv = warp != kProdWarp;
+    if (lane == 0 && !pv) {
+      // the Q tiles first (after the barrier set-up above is visible): two
+      // 64-column SWIZZLE_128B atoms per tile, the S MMA's A layout
+      for (int x = 0; x < nq; ++x) {
+        mbar_arrive_expect_tx(&bars[bQReady + x], static_cast<uint32_t>(kQTile));
+        tma_load_3d(sbase + kOffQ + x * kQTile, &a.tm_q, h * D, q0 + x * BM, b, &bars[bQReady + x]);
+        tma_load_3d(sbase + kOffQ + x * kQTile + kQAtom, &a.tm_q, h * D + 64, q0 + x * BM, b, &bars[bQReady + x]);
+      }
+    }
     if (lane == 0) {
       const CUtensorMap* tc = pv ? &a.tm_vc : &a.tm_kc;
       const CUtensorMap* tsk = pv ? &a.tm_vs : &a.tm_ks;
@@ -916,6 +901,10 @@ static int attention_impl(const void* q, int64_t q_token_stride, const void* k_c
                         (uint64_t)n_heads * 256, srows, 64, attn::BN, CU_TENSOR_MAP_SWIZZLE_128B, "v sink");
     if (rc) return rc;
   }
+  rc = attn::make_out_map(&a.tm_q, const_cast<void*>(q), static_cast<uint64_t>(n_heads) * head_dim,
+                          static_cast<uint64_t>(q_token_stride), static_cast<uint64_t>(n_q),
+                          static_cast<uint64_t>(batch));
+  if (rc) return rc;
   a.q = static_cast<const uint16_t*>(q);
   a.q_tok_stride = q_token_stride;
   a.q_batch_stride = q_token_stride * n_q;
