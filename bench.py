@@ -61,12 +61,17 @@ _REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_
 
 class ClockSampler:
     """Samples SM clock and clock-event reasons of one GPU (NVML, read-only) in a
-    background thread while the timed region runs."""
+    background thread, as fast as NVML answers. mark_start() / mark_end() bracket
+    the timed region (host clock, right before the start event is recorded and
+    right after the closing synchronize); the summary keeps the samples inside
+    it, and when a short region holds fewer than 3 samples, also the ones
+    within 50 ms of it (and says so)."""
 
-    def __init__(self, device: int, period_s: float = 0.02):
+    def __init__(self, device: int, period_s: float = 0.0005):
         self.period = period_s
-        self.samples: list[tuple[int, int, float]] = []
+        self.samples: list[tuple[float, int, int, float]] = []
         self.max_mhz = None
+        self.t0 = self.t1 = None
         self._stop = threading.Event()
         self._h = None
         try:
@@ -83,6 +88,7 @@ class ClockSampler:
 
     def _run(self):
         nv = self._nv
+        n = 0
         while not self._stop.is_set():
             try:
                 mhz = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
@@ -90,18 +96,28 @@ class ClockSampler:
                     rs = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
                 except Exception:
                     rs = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self._h)
-                pw = nv.nvmlDeviceGetPowerUsage(self._h) / 1000.0
-                self.samples.append((mhz, rs, pw))
+                pw = nv.nvmlDeviceGetPowerUsage(self._h) / 1000.0 if n % 8 == 0 else float("nan")
+                self.samples.append((time.perf_counter(), mhz, rs, pw))
+                n += 1
             except Exception:
                 pass
             time.sleep(self.period)
 
+    def mark_start(self):
+        self.t0 = time.perf_counter()
+
+    def mark_end(self):
+        self.t1 = time.perf_counter()
+
     def __enter__(self):
         if self._h is not None:
             self._t.start()
+            time.sleep(0.05)
         return self
 
     def __exit__(self, *exc):
+        if self._h is not None:
+            time.sleep(0.05)
         self._stop.set()
         if self._h is not None:
             self._t.join(timeout=2)
@@ -110,13 +126,24 @@ class ClockSampler:
         if not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0,
                     "source": "nvml unavailable" if self._h is None else "nvml"}
-        mhz = [s[0] for s in self.samples]
+        t0 = self.t0 if self.t0 is not None else -math.inf
+        t1 = self.t1 if self.t1 is not None else math.inf
+        sel = [x for x in self.samples if t0 <= x[0] <= t1]
+        window = "timed region"
+        if len(sel) < 3:
+            sel = [x for x in self.samples if t0 - 0.05 <= x[0] <= t1 + 0.05]
+            window = "timed region +- 50 ms (the region is shorter than 3 samples)"
+        if not sel:
+            sel = self.samples
+            window = "whole run"
+        mhz = [x[1] for x in sel]
         bits = 0
-        for s in self.samples:
-            bits |= int(s[1])
+        for x in sel:
+            bits |= int(x[2])
         reasons = sorted(n for b, n in _REASONS.items() if bits & b and n != "gpu_idle")
+        pw = [x[3] for x in sel if x[3] == x[3]]
         return {"sm_mhz": float(statistics.median(mhz)), "sm_max_mhz": self.max_mhz, "reasons": reasons,
-                "samples": len(mhz), "power_w_max": round(max(s[2] for s in self.samples), 1),
+                "samples": len(mhz), "window": window, "power_w_max": round(max(pw), 1) if pw else None,
                 "source": "nvml"}
 
 
@@ -278,9 +305,11 @@ def run_ours(args):
         out = torch.empty_like(q)
         sets.append((q, tk, tv, out))
         if fused:
-            # full-width output of the set on every rank, mapped into every peer
+            # full-width output of the set on every rank, mapped into every peer, with
+            # a completion counter per rank (device-side signal, no host barrier)
             peers.append(shard.PeerOutputs(torch.empty((B, LQ, H_TOTAL, D), dtype=torch.bfloat16, device=dev)))
     gbuf = shard.gather_buffer(sets[0][3], world) if world > 1 else None
+    step_tiles = world * ops.gather_tiles(B, LQ, Hl)     # output tiles all ranks store per step
     torch.cuda.synchronize()
 
     def step(i, kev=None):
@@ -288,12 +317,18 @@ def run_ours(args):
         if kev is not None:
             kev[0].record()
         if fused:
-            ops.attention_packed_gather(q, tk, tv, 0, LK, peers[i % N_SETS].ptrs, h0, H_TOTAL)
+            po = peers[i % N_SETS]
+            ops.attention_packed_gather(q, tk, tv, 0, LK, po.ptrs, h0, H_TOTAL, signals=po.sig_ptrs)
         else:
             ops.attention_packed(q, tk, tv, 0, LK, out=out)
         if kev is not None:
             kev[1].record()
-        if world > 1 and not fused:
+        if fused:
+            # the step's consumer may read po.local once every rank's tiles have landed:
+            # a stream-ordered wait on this GPU's counter (part of the timed step)
+            po.expect(step_tiles)
+            po.wait()
+        elif world > 1:
             shard.gather_outputs(out, gbuf)
 
     for i in range(args.warmup):
@@ -305,11 +340,13 @@ def run_ours(args):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
         torch.cuda.synchronize()
+        clk.mark_start()
         e0.record()
         for i in range(args.steps):
             step(i, kevs[i])
         e1.record()
         torch.cuda.synchronize()
+        clk.mark_end()
     if world > 1:
         dist.barrier()
     t_ms = max_over_ranks(e0.elapsed_time(e1), world, dev)
@@ -318,6 +355,9 @@ def run_ours(args):
     status = ops.device_status()
     if status != 0:
         raise SystemExit(f"device status {status}: a kernel wait timed out; results invalid")
+    gather_check = None
+    if world > 1:
+        gather_check = check_gather(sets, peers, fused, gbuf, step, args.warmup + args.steps, world, dev)
     flops_rank = attn_flops(B, Hl, LQ, LK)
     value = world * flops_rank * args.steps / (t_ms / 1e3) / 1e12
     achieved = flops_rank / (k_mean / 1e3) / 1e12
@@ -329,6 +369,8 @@ def run_ours(args):
     cpu = None
     if world == 1 and not args.no_extras:
         extra = run_extras(dev, peaks)
+    if not args.no_config4:
+        extra["config4"] = run_config4(args, dev, world, rank, peaks)
     if rank == 0 and world == 1 and not args.no_cpu:
         times, threads = cpu_attention_sample(2, min_seconds=args.cpu_seconds, warmup=1)
         per = sum(times) / len(times)
@@ -350,13 +392,17 @@ def run_ours(args):
                      "kernel_ms": k_mean,
                      "peak_source": f"{peaks['source']} bf16 dense (burst), of {peaks['source']}"},
         "e2e": e2e,
-        "gpu_launches": args.steps,
+        "gpu_launches": args.steps * (2 if fused else 1),
         "clocks": clk.summary(),
         "cpu_baseline": cpu,
         "extra": extra,
     }
+    if gather_check is not None:
+        line["gather_check"] = gather_check
     if rank == 0:
         print(json.dumps(line), flush=True)
+    if gather_check is False:
+        raise SystemExit("gather_check failed: a rank's gathered output differs from the NCCL-gathered outputs")
     if world > 1:
         dist.barrier()          # every rank is done storing into the peers' buffers
         for p in peers:
@@ -365,35 +411,75 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def check_gather(sets, peers, fused, gbuf, step, i, world, dev) -> bool:
+    """Untimed step i (set i % N_SETS) after the timing; every rank then compares
+    the full output it holds with the ranks' own attention outputs gathered by
+    NCCL, bit for bit. The verdict is the AND over the ranks."""
+    import torch.distributed as dist
+    from kvq import ops, shard
+    q, tk, tv, out = sets[i % N_SETS]
+    full = peers[i % N_SETS].local if fused else None
+    if fused:
+        full.zero_()
+        torch.cuda.synchronize()
+        dist.barrier()
+    step(i)
+    if fused:
+        got = full.clone()
+    else:
+        got = shard.assemble_heads(gbuf.view(world, *out.shape)).clone()
+    ref = shard.assemble_heads(shard.gather_outputs(ops.attention_packed(q, tk, tv, 0, LK)))
+    ok = torch.tensor([1 if torch.equal(got, ref) and ops.device_status() == 0 else 0], device=dev)
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    torch.cuda.synchronize()
+    dist.barrier()
+    return bool(ok.item())
+
+
 def run_e2e(args, dev, world, B, Hl, h0, gbuf):
-    """Same metric through quant_kv (the drop-in API), from host memory: per step,
-    copy q, k, v of the block from pinned host memory, quantize-append K and V
-    into the caches (slice write), attention over the window, copy the output
-    back to the host. Three streams pipeline consecutive steps (upload of step
-    i+1 and download of step i-1 overlap the compute of step i); every step still
-    moves all of its inputs and its output across PCIe inside the timed region."""
+    """Same metric through the public API, from host memory: per step, copy q, k,
+    v of the block from pinned host memory, quantize-append K and V into the
+    caches (QuantKVTensor slice writes), attention over the window
+    (quant_kv.attention on one GPU; at N > 1 the head-sharded
+    ops.attention_packed_gather into PeerOutputs with its device-side completion
+    wait), and copy the step's result back to the host (N = 1: the output; N > 1:
+    the full output of the stream this rank serves, all 40 heads). Three streams
+    pipeline consecutive steps (upload of step i+1 and download of step i-1
+    overlap the compute of step i); every step still moves all of its inputs and
+    its output across PCIe inside the timed region."""
     import quant_kv
-    from kvq import shard, synth
+    from kvq import ops, shard, synth
     tk = quant_kv.QuantKVTensor([B, LK, Hl, D], dev, torch.bfloat16, 4, MODE, SINK)
     tv = quant_kv.QuantKVTensor([B, LK, Hl, D], dev, torch.bfloat16, 4, MODE, SINK)
-    nb = 2
+    nb = 2          # input buffers
+    no = 3          # output buffers: a peer may store into buffer i % 3 once this rank's
+                    # download of step i - 3 is done (the compute of step i - 1 waited for it)
     qh = [synth.make_q(B, LQ, Hl, seed=11 + i).pin_memory() for i in range(nb)]
     kh = [torch.stack([synth.make_k(LK, Hl, seed=12 + b + i) for b in range(B)]).pin_memory() for i in range(nb)]
     vh = [torch.stack([synth.make_v(LK, Hl, seed=13 + b + i) for b in range(B)]).pin_memory() for i in range(nb)]
-    oh = [torch.empty((B, LQ, Hl, D), dtype=torch.bfloat16).pin_memory() for _ in range(nb)]
     qd = [torch.empty_like(qh[0], device=dev) for _ in range(nb)]
     kd = [torch.empty_like(kh[0], device=dev) for _ in range(nb)]
     vd = [torch.empty_like(vh[0], device=dev) for _ in range(nb)]
-    od = [torch.empty_like(qd[0]) for _ in range(nb)]
+    if world == 1:
+        od = [torch.empty((B, LQ, Hl, D), dtype=torch.bfloat16, device=dev) for _ in range(no)]
+        res = od
+        pos = None
+    else:
+        rank = int(os.environ.get("RANK", "0"))
+        pos = [shard.PeerOutputs(torch.empty((B, LQ, H_TOTAL, D), dtype=torch.bfloat16, device=dev))
+               for _ in range(no)]
+        res = [p.local[rank] for p in pos]              # [LQ, 40, D]: the stream this rank serves
+    oh = [torch.empty(res[0].shape, dtype=torch.bfloat16).pin_memory() for _ in range(no)]
+    step_tiles = world * ops.gather_tiles(B, LQ, Hl)
     s_up, s_cmp, s_dn = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     ev = lambda: torch.cuda.Event()  # noqa: E731
     up_done, cmp_done, dn_done = {}, {}, {}
 
     def step(i):
-        j = i % nb
+        j, o = i % nb, i % no
         with torch.cuda.stream(s_up):
             if i - nb in cmp_done:
-                s_up.wait_event(cmp_done[i - nb])      # step i-2 finished reading buffer j
+                s_up.wait_event(cmp_done[i - nb])      # step i-2 finished reading input buffer j
             qd[j].copy_(qh[j], non_blocking=True)
             kd[j].copy_(kh[j], non_blocking=True)
             vd[j].copy_(vh[j], non_blocking=True)
@@ -401,23 +487,27 @@ def run_e2e(args, dev, world, B, Hl, h0, gbuf):
             up_done[i].record(s_up)
         with torch.cuda.stream(s_cmp):
             s_cmp.wait_event(up_done[i])
-            if i - nb in dn_done:
-                s_cmp.wait_event(dn_done[i - nb])      # output buffer j downloaded
+            if i - 2 in dn_done:
+                s_cmp.wait_event(dn_done[i - 2])       # output buffer (i-2) % 3 downloaded
             tk[:, 0:LK] = kd[j]
             tv[:, 0:LK] = vd[j]
-            quant_kv.attention(qd[j], tk[:, 0:LK], tv[:, 0:LK], out=od[j])
-            if world > 1:
-                shard.gather_outputs(od[j], gbuf)
+            if pos is None:
+                quant_kv.attention(qd[j], tk[:, 0:LK], tv[:, 0:LK], out=od[o])
+            else:
+                po = pos[o]
+                ops.attention_packed_gather(qd[j], tk, tv, 0, LK, po.ptrs, h0, H_TOTAL, signals=po.sig_ptrs)
+                po.expect(step_tiles)
+                po.wait()
             cmp_done[i] = ev()
             cmp_done[i].record(s_cmp)
         with torch.cuda.stream(s_dn):
             s_dn.wait_event(cmp_done[i])
-            oh[j].copy_(od[j], non_blocking=True)
+            oh[o].copy_(res[o], non_blocking=True)
             dn_done[i] = ev()
             dn_done[i].record(s_dn)
 
     n = max(3, min(args.steps, 20))
-    for i in range(max(2, args.warmup)):
+    for i in range(max(3, args.warmup)):
         step(i)
     torch.cuda.synchronize()
     if world > 1:
@@ -432,13 +522,21 @@ def run_e2e(args, dev, world, B, Hl, h0, gbuf):
     e1.record(s_up)
     torch.cuda.synchronize()
     t = max_over_ranks(e0.elapsed_time(e1), world, dev)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()              # every rank is done storing into and reading the buffers
+        for p in pos:
+            p.close()
+        dist.barrier()
     flops = world * attn_flops(B, Hl, LQ, LK) * n
     h2d = (qh[0].numel() + kh[0].numel() + vh[0].numel()) * 2
     return {"value": flops / (t / 1e3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": oh[0].numel() * 2, "steps": n, "ms_per_step": t / n,
-            "path": "pinned H2D of q,k,v -> QuantKVTensor slice writes (quantize-append) -> "
-                    "quant_kv.attention -> D2H of the output; upload, compute and download of "
-                    "consecutive steps on three streams"}
+            "path": ("pinned H2D of q,k,v -> QuantKVTensor slice writes (quantize-append) -> "
+                     + ("quant_kv.attention" if world == 1 else
+                        "ops.attention_packed_gather (all-gather in the epilogue) + device-side completion wait")
+                     + " -> D2H of the step's output; upload, compute and download of consecutive steps on "
+                       "three streams")}
 
 
 def _time_events(fn, n, warm=2):
@@ -508,23 +606,43 @@ def run_extras(dev, peaks):
     del xs, cs, ss
     torch.cuda.empty_cache()
 
-    # the append of one block to all 40 layers x {K, V} in one launch (kvq_rebuild_layers)
+    # the append of one layer's block (K and V, 4680 tokens x 40 heads) as ONE launch
+    # (kvq_rebuild_layers with the two tensors): the runtime's per-layer pattern
+    xs = [synth.make_k(LK, H_TOTAL, seed=650 + i, device=dev) for i in range(8)]
+    cs = [torch.empty((LK, H_TOTAL, D // 2), dtype=torch.uint8, device=dev) for _ in range(8)]
+    ss = [torch.empty((LK, H_TOTAL, G), dtype=torch.bfloat16, device=dev) for _ in range(8)]
+
+    def fl(i):
+        j = 2 * (i % 4)
+        ops.quantize_layers_into(xs[j:j + 2], cs[j:j + 2], ss[j:j + 2], cb, G, 4)
+    ms = _time_events(fl, 20)
+    byts = 2 * LK * H_TOTAL * quant_bytes_per_row(G)
+    gbs = byts / (statistics.median(ms) / 1e3) / 1e9
+    res["quantize_append_layer_kv_4680_one_launch"] = {
+        "gbs": gbs, "ms": statistics.median(ms), "bytes": byts, "frac_hbm": gbs / peaks["hbm_gbs"],
+        "note": "4 rotating input pairs (384 MB > L2)"}
+    del xs, cs, ss
+    torch.cuda.empty_cache()
+
+    # the append of one block to all 40 layers x {K, V} in one launch (kvq_rebuild_layers),
+    # 80 distinct inputs (3.8 GB), so no input is re-read from L2
     nt = 80
-    xs = [synth.make_k(LK, H_TOTAL, seed=700 + (i % 8), device=dev) for i in range(8)]
+    xs = [synth.make_k(LK, H_TOTAL, seed=700 + i, device=dev) for i in range(nt)]
     cs = [torch.empty((LK, H_TOTAL, D // 2), dtype=torch.uint8, device=dev) for _ in range(nt)]
     ss = [torch.empty((LK, H_TOTAL, G), dtype=torch.bfloat16, device=dev) for _ in range(nt)]
-    xin = [xs[i % 8] for i in range(nt)]
 
     def fb(_i):
-        ops.quantize_layers_into(xin, cs, ss, cb, G, 4)
+        ops.quantize_layers_into(xs, cs, ss, cb, G, 4)
     ms = _time_events(fb, 10)
     byts = nt * LK * H_TOTAL * quant_bytes_per_row(G)
     gbs = byts / (statistics.median(ms) / 1e3) / 1e9
     res["quantize_append_40layers_kv_4680_one_launch"] = {
         "gbs": gbs, "ms": statistics.median(ms), "bytes": byts, "frac_hbm": gbs / peaks["hbm_gbs"],
-        "note": "8 distinct inputs cycled over the 80 tensors (inputs 384 MB > L2)"}
-    del xs, cs, ss, xin
+        "note": "80 distinct inputs (3.8 GB)"}
+    del xs, cs, ss
     torch.cuda.empty_cache()
+
+    res["window21_block"] = run_window21_block(dev, peaks)
 
     # eviction in a window-21 cache (one layer's K and V): the 2 oldest frames after the
     # sink leave, `kv[:, a:b] = kv[:, c:d].clone()` moves the rest down; the reference's
@@ -595,6 +713,162 @@ def run_extras(dev, peaks):
     return res
 
 
+def run_window21_block(dev, peaks):
+    """One block of the resident runtime at window 21 (32,760 tokens, a 1,560-token
+    sink), 40 layers, one stream, 40 heads (quant_kv.py:12-14): per layer
+      1. rolling eviction of the oldest block after the sink, K and V:
+         kv[:, 1560:28080] = kv[:, 6240:32760].clone() (the reference's
+         dequantize + requantize; lossless_moves copies packed rows instead)
+      2. append of the new 4,680-token block: keys before their rotary embedding
+         through the fused rotate + quantize (write_rope_), values by slice write
+      3. attention of the block's 4,680 queries over the window.
+    Reported per block, with the phases also timed alone."""
+    import quant_kv
+    from kvq import ops, rope, synth
+    S, NB, layers = 21 * FRAME, 3 * FRAME, 40
+    fr = rope.freqs(1024, device=dev)
+    pos = rope.grid_positions(S, NB, device=dev)
+    res = {}
+    k_fill = synth.make_k(S, H_TOTAL, seed=800, device=dev)
+    v_fill = synth.make_v(S, H_TOTAL, seed=801, device=dev)
+    kpre = [synth.make_v(NB, H_TOTAL, seed=810 + i, device=dev) for i in range(layers)]   # keys before rotation
+    vnew = [synth.make_v(NB, H_TOTAL, seed=860 + i, device=dev) for i in range(layers)]
+    qs = [synth.make_q(1, NB, H_TOTAL, seed=910 + i, device=dev) for i in range(layers)]
+    out = torch.empty((1, NB, H_TOTAL, D), dtype=torch.bfloat16, device=dev)
+    for lossless in (False, True):
+        caches = []
+        for _ in range(layers):
+            ck = quant_kv.QuantKVTensor([1, S, H_TOTAL, D], dev, torch.bfloat16, 4, MODE, SINK, lossless)
+            cv = quant_kv.QuantKVTensor([1, S, H_TOTAL, D], dev, torch.bfloat16, 4, MODE, SINK, lossless)
+            quant_kv.write_layers([ck, cv], [k_fill, v_fill], 0, S)
+            caches.append((ck, cv))
+
+        def evict(layer):
+            for c in caches[layer]:
+                c[:, SINK:S - NB] = c[:, SINK + NB:S].clone()
+
+        def append(layer):
+            ck, cv = caches[layer]
+            ck.write_rope_(S - NB, S, kpre[layer], fr, pos)
+            cv[:, S - NB:S] = vnew[layer]
+
+        def attend(layer):
+            ck, cv = caches[layer]
+            quant_kv.attention(qs[layer], ck[:, 0:S], cv[:, 0:S], out=out)
+
+        def block(_i, phases=(evict, append, attend)):
+            for layer in range(layers):
+                for f in phases:
+                    f(layer)
+        ms = min(_time_events(block, 2, warm=1))
+        parts = {name: min(_time_events(lambda _i, f=f: block(_i, (f,)), 2, warm=1))
+                 for name, f in (("evict", evict), ("append", append), ("attention", attend))}
+        fl = layers * attn_flops(1, H_TOTAL, NB, S)
+        res["lossless" if lossless else "requantize"] = {
+            "ms_per_block": ms, "phase_ms": parts, "attention_tflops": fl / (parts["attention"] / 1e3) / 1e12}
+        del caches
+        torch.cuda.empty_cache()
+    res["workload"] = ("window 21, 40 layers, 1 stream x 40 heads; per layer: eviction of 4680 tokens after the "
+                       "1560-token sink (K and V), rotate+quantize append of the new block's keys, append of its "
+                       "values, attention of its 4680 queries over the 32760-token window")
+    return res
+
+
+def run_config4(args, dev, world, rank, peaks):
+    """The head-sharded workload, strong scaling: window 21 (32,760 tokens, a
+    1,560-token sink), 40 layers, 4 independent streams, the 40 heads split
+    40/20/10/5 over 1/2/4/8 GPUs. Per block and layer: append of the new
+    4,680-token block of K and V at the ring's end (one launch for K and V of the
+    4 streams), then attention of the block's 4 x 4,680 queries over the window;
+    at N > 1 the attention's epilogue all-gathers the output into every rank
+    (alternating two PeerOutputs), and the layer ends with the device-side wait
+    for every rank's tiles (what the next layer's input needs). Timed with CUDA
+    events, max over ranks; the total work is the same at every N."""
+    import quant_kv
+    from kvq import ops, shard, synth
+    B, S, NB, layers = 4, 21 * FRAME, 3 * FRAME, 40
+    h0, h1 = shard.head_range(H_TOTAL, world, rank)
+    Hl = h1 - h0
+    caches, ks, vs, qs = [], [], [], []
+    # the window's contents: one synthetic K and V per stream, quantized into every layer
+    k_fill = torch.stack([synth.make_k(S, Hl, seed=2000 + 101 * b + h0, device=dev) for b in range(B)])
+    v_fill = torch.stack([synth.make_v(S, Hl, seed=2001 + 101 * b + h0, device=dev) for b in range(B)])
+    for layer in range(layers):
+        ck = quant_kv.QuantKVTensor([B, S, Hl, D], dev, torch.bfloat16, 4, MODE, SINK)
+        cv = quant_kv.QuantKVTensor([B, S, Hl, D], dev, torch.bfloat16, 4, MODE, SINK)
+        quant_kv.write_layers([ck, cv], [k_fill, v_fill], 0, S)
+        caches.append((ck, cv))
+        # the new block of every layer: distinct inputs (> L2 in total at every N)
+        ks.append(torch.stack([synth.make_k(NB, Hl, seed=3000 + 7 * layer + b + h0, pos0=S, device=dev)
+                               for b in range(B)]))
+        vs.append(torch.stack([synth.make_v(NB, Hl, seed=4000 + 7 * layer + b + h0, device=dev) for b in range(B)]))
+        qs.append(synth.make_q(B, NB, Hl, seed=5000 + layer + h0, device=dev))
+    del k_fill, v_fill
+    if world == 1:
+        outs = [torch.empty((B, NB, H_TOTAL, D), dtype=torch.bfloat16, device=dev) for _ in range(2)]
+        pos = None
+    else:
+        pos = [shard.PeerOutputs(torch.empty((B, NB, H_TOTAL, D), dtype=torch.bfloat16, device=dev))
+               for _ in range(2)]
+    step_tiles = world * ops.gather_tiles(B, NB, Hl)
+    torch.cuda.synchronize()
+
+    def block():
+        for layer in range(layers):
+            ck, cv = caches[layer]
+            quant_kv.write_layers([ck, cv], [ks[layer], vs[layer]], S - NB, S)
+            if pos is None:
+                ops.attention_packed(qs[layer], ck, cv, 0, S, out=outs[layer % 2])
+            else:
+                po = pos[layer % 2]
+                ops.attention_packed_gather(qs[layer], ck, cv, 0, S, po.ptrs, h0, H_TOTAL, signals=po.sig_ptrs)
+                po.expect(step_tiles)
+                po.wait()
+
+    n_blocks = 2
+    block()                                   # warm-up
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(n_blocks):
+        block()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1), world, dev) / n_blocks
+    status = ops.device_status()
+    flops = layers * attn_flops(B, H_TOTAL, NB, S)
+    abytes = layers * 2 * B * NB * H_TOTAL * quant_bytes_per_row(len(quant_kv._band_edges(D, MODE)))
+    res = {"workload": "window 21 (32760 tokens, 1560-token sink), 40 layers, 4 streams; per layer: append of "
+                       "a 4680-token block (K and V) + attention of 4x4680 queries over the window"
+                       + ("" if world == 1 else ", output all-gathered in the attention epilogue + device-side "
+                          "completion wait"),
+           "scaling": "strong", "heads_per_gpu": Hl, "n_gpus": world, "ms_per_block": ms,
+           "attention_tflops": flops / (ms / 1e3) / 1e12, "append_bytes_per_block": abytes,
+           "frac_of_bf16_peak": flops / (ms / 1e3) / 1e12 / peaks["bf16_tflops_sustained"],
+           "peak": "sustained bf16 (a block runs for a second and more), of " + peaks["source"],
+           "device_status": status}
+    if world > 1:
+        # the last layer's gathered output against the ranks' own outputs gathered by NCCL
+        import torch.distributed as dist
+        last = layers - 1
+        ck, cv = caches[last]
+        ref = shard.assemble_heads(shard.gather_outputs(ops.attention_packed(qs[last], ck, cv, 0, S)))
+        ok = torch.tensor([1 if torch.equal(pos[last % 2].local, ref) and status == 0 else 0], device=dev)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        res["gather_check"] = bool(ok.item())
+        torch.cuda.synchronize()
+        dist.barrier()
+        for p in pos:
+            p.close()
+        dist.barrier()
+    del caches, ks, vs, qs
+    torch.cuda.empty_cache()
+    return res
+
+
 def run_profile_case(case: str, launches: int = 6):
     """A small single-GPU case for ncu captures: a few launches of one kernel on
     inputs larger than L2, nothing else."""
@@ -633,6 +907,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--no-extras", action="store_true", help="skip quantize / prefill extras")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--no-config4", action="store_true",
+                    help="skip the window-21 / 40-layer / 4-stream head-sharded block")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--gather", default="fused", choices=("fused", "nccl"),
                     help="N > 1: all-gather of the output in the attention epilogue, or by NCCL")

@@ -45,7 +45,7 @@ extern "C" {
 #define KVQ_ERR_DEVICE (-5)      /* the current device is not an sm_100 part */
 
 /* ABI version of this header; bumped on any signature change. */
-#define KVQ_ABI_VERSION 2
+#define KVQ_ABI_VERSION 3
 
 /* Size of the opaque handle kvq_ipc_export() writes (a cudaIpcMemHandle_t). */
 #define KVQ_IPC_HANDLE_BYTES 64
@@ -179,6 +179,12 @@ KVQ_API int kvq_rebuild_layers(int n_tensors, const void* const* x, int64_t x_to
  * With outs = every rank's output buffer (peers mapped by kvq_ipc_import()),
  * the epilogue is the all-gather of the output over NVLink: when every rank's
  * launch has completed, every rank holds the full [batch, n_q, out_heads, D].
+ * signals: NULL, or n_outs counters (unsigned 32-bit, 4-byte aligned), signals[d]
+ * in the memory of destination d (peers mapped like the outputs): every 128-row
+ * output tile, once its stores have landed in all destinations, adds 1 to each
+ * destination's counter with release semantics at system scope. A launch adds
+ * batch * n_heads * ceil(n_q / 128) to each counter; a consumer waits with
+ * kvq_gather_wait() for the sum over all ranks' launches of a step.
  * Other arguments and errors as kvq_attention(). No counterpart in the
  * reference (single GPU); replaces the attention + NCCL all-gather pair of a
  * head-sharded deployment.
@@ -187,10 +193,22 @@ KVQ_API int kvq_attention_gather(const void* q, int64_t q_token_stride,
                                  const void* k_codes, const void* k_scales, const void* k_sink,
                                  const void* v_codes, const void* v_scales, const void* v_sink,
                                  int64_t cache_tokens, int64_t sink_tokens, int64_t lo, int64_t hi,
-                                 void* const* outs, int n_outs, int out_head0, int out_heads,
+                                 void* const* outs, unsigned int* const* signals, int n_outs,
+                                 int out_head0, int out_heads,
                                  int64_t out_token_stride, int batch, int64_t n_q,
                                  int n_heads, int head_dim, const int32_t* chan_band, int n_groups,
                                  int k_bits, int v_bits, float softmax_scale, void* stream);
+
+/*
+ * Stream-ordered wait for a gather's completion: one thread on `stream` waits
+ * until *counter (this GPU's signal counter of kvq_attention_gather()) reaches
+ * target, compared modulo 2^32 (a difference below 2^31 counts as reached), so
+ * that work launched after it on the stream reads the gathered output without a
+ * host barrier. Gives up after wait_cycles (>= 1000, at most about a second),
+ * raising the device status word (kvq_device_status()). No counterpart in the
+ * reference (single GPU).
+ */
+KVQ_API int kvq_gather_wait(const unsigned int* counter, unsigned int target, int64_t wait_cycles, void* stream);
 
 /*
  * CUDA IPC for the output buffers of kvq_attention_gather(). kvq_ipc_export()
@@ -203,6 +221,25 @@ KVQ_API int kvq_attention_gather(const void* q, int64_t q_token_stride,
 KVQ_API int kvq_ipc_export(const void* ptr, void* handle, int64_t* offset);
 KVQ_API int kvq_ipc_import(const void* handle, int64_t offset, void** base, void** ptr);
 KVQ_API int kvq_ipc_close(void* base);
+
+/*
+ * Test hook of the bounded waits (no counterpart in the reference, whose Triton
+ * kernels have no waits): kvq_attention() with the K tiles from stall_tile on
+ * withheld by the producer and every wait limited to wait_cycles (>= 1000 and at
+ * most the default of about a second). The waits for the withheld tile give up,
+ * the kernel raises the device status word (kvq_device_status() returns 1), lets
+ * its in-flight copies and MMAs finish, frees its tensor memory and returns; the
+ * output is invalid. Used by the tests to show that a timed-out launch leaves
+ * the context usable.
+ */
+KVQ_API int kvq_test_attention_timeout(const void* q, int64_t q_token_stride,
+                                       const void* k_codes, const void* k_scales, const void* k_sink,
+                                       const void* v_codes, const void* v_scales, const void* v_sink,
+                                       int64_t cache_tokens, int64_t sink_tokens, int64_t lo, int64_t hi,
+                                       void* out, int64_t out_token_stride, int batch, int64_t n_q,
+                                       int n_heads, int head_dim, const int32_t* chan_band, int n_groups,
+                                       int k_bits, int v_bits, float softmax_scale, int stall_tile,
+                                       int64_t wait_cycles, void* stream);
 
 /*
  * Synchronizes the current device and returns the library's device status word:

@@ -129,10 +129,13 @@ struct alignas(64) Args {
   uint16_t* out[kMaxOut];  // n_out destinations of identical layout (this GPU's and peers')
   int n_out, out_head0;     // heads of this launch land at heads out_head0.. of each destination
   int tma_out;              // store through tm_out (one TMA store per Q tile and destination)
+  unsigned* sig[kMaxOut];   // or NULL: completion counter of destination d (in d's memory), +1 per Q tile stored
   float* stats;             // STATS kernels: [batch][n_q][n_heads][4] fp32 row statistics
   CUtensorMap tm_out[kMaxOut];  // destination d as [batch][n_q][out_heads * D] bf16, box 64 x 128 x 1, SWIZZLE_128B
   int64_t o_tok_stride, o_batch_stride;
   float scale_log2;
+  long long wait_cycles;  // limit of every bounded wait (kWaitCycles unless a test asks for less)
+  int stall_tile;         // >= 0 only in the abort test: the K producer stops before this KV tile
 };
 
 // byte offset of 16-byte chunk c (8 bf16 columns) of row r in a 64 x 128 bf16
@@ -297,6 +300,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
+  const long long lim = a.wait_cycles;
   // One CTA per (pair of Q tiles, head, stream), 1-D grid. The CTAs with two Q
   // tiles come first, pairs fastest (a head's packed K/V stays in L2 across its
   // pairs); the last pairs that hold at most BM queries (one Q tile, about half
@@ -380,7 +384,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
     auto step = [&](const int j, const int valid, auto part) -> bool {
       constexpr bool PART = decltype(part)::value;
       const uint32_t tS = tS0 + 64 * (j & 1);
-      if (!mbar_wait_warp(&bars[bSFull + 2 * x + (j & 1)], (j >> 1) & 1, abort, &g_attn_status)) return false;
+      if (!mbar_wait_warp(&bars[bSFull + 2 * x + (j & 1)], (j >> 1) & 1, abort, &g_attn_status, lim)) return false;
       // S_x(j) complete => this Q tile no longer reads K stage j, and PV_x(j-2)
       // (issued before it) is complete: nor V stage j-2
       if ((warp & 3) == 0 && lane == 0) {
@@ -429,7 +433,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
         // at the last tile, for the commit that follows PV_x(j-1).
         const bool last = j + 1 == nkv;
         if (!mbar_wait_warp(&bars[last ? bOReady + x : bSFull + 2 * x + ((j + 1) & 1)],
-                            last ? 0u : static_cast<uint32_t>(((j + 1) >> 1) & 1), abort, &g_attn_status))
+                            last ? 0u : static_cast<uint32_t>(((j + 1) >> 1) & 1), abort, &g_attn_status, lim))
           return false;
         tc_fence_after();
 #pragma unroll 1
@@ -494,7 +498,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
         break;
       }
     }
-    if (ok && mbar_wait_warp(&bars[bOFinal + x], 0, abort, &g_attn_status)) {
+    if (ok && mbar_wait_warp(&bars[bOFinal + x], 0, abort, &g_attn_status, lim)) {
       tc_fence_after();
       const float inv = 1.0f / l;
       if (STATS && qi < a.Lq) {
@@ -530,14 +534,24 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars[bEpi + x]);
-        if ((warp & 3) == 0 && lane == 0 && mbar_wait(&bars[bEpi + x], 0, abort, &g_attn_status)) {
+        if ((warp & 3) == 0 && lane == 0 && mbar_wait(&bars[bEpi + x], 0, abort, &g_attn_status, lim)) {
           const int xq = (a.out_head0 + h) * D, yq = q0 + x * BM;
           for (int d = 0; d < a.n_out; ++d) {
             tma_store_3d(&a.tm_out[d], stage, xq, yq, b);
             tma_store_3d(&a.tm_out[d], stage + kQAtom, xq + 64, yq, b);
           }
           bulk_commit();
-          bulk_wait_read_all();  // the staging buffer must outlive the reads
+          if (a.sig[0]) {
+            // completion signal of the gather: once this tile's stores have landed
+            // in every destination, add 1 to each destination's counter (release,
+            // system scope), so a consumer that acquires count >= its target reads
+            // every row without a host barrier
+            bulk_wait_all();
+            fence_proxy_async_global();
+            for (int d = 0; d < a.n_out; ++d) red_release_sys_add(a.sig[d], 1u);
+          } else {
+            bulk_wait_read_all();  // the staging buffer must outlive the reads
+          }
         }
         __syncwarp();
       } else {
@@ -595,9 +609,9 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
       const bool coded = live && tok >= a.sink_tokens;
       const ScaleWords<L> sw = sw_next;
       load_sw(j + 1, sw_next);
-      if (!mbar_wait_warp(&bars[bLdFull + is_v * NS_LD + ls], (j / NS_LD) & 1, abort, &g_attn_status)) break;
+      if (!mbar_wait_warp(&bars[bLdFull + is_v * NS_LD + ls], (j / NS_LD) & 1, abort, &g_attn_status, lim)) break;
       if (j >= NS_KV &&
-          !mbar_wait_warp(&bars[bKvEmpty + is_v * NS_KV + ks], ((j / NS_KV) - 1) & 1, abort, &g_attn_status))
+          !mbar_wait_warp(&bars[bKvEmpty + is_v * NS_KV + ks], ((j / NS_KV) - 1) & 1, abort, &g_attn_status, lim))
         break;
       const uint32_t dst = kv_base + ks * kKVTile;
       if (!live) {
@@ -654,16 +668,19 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
       const uint32_t code_base = sbase + (pv ? kOffVC : kOffKC);
       const uint32_t kv_base = sbase + (pv ? kOffV : kOffK);
       const int code_x = h * (pv ? 64 : (KB == 4 ? 64 : 128));
+      int issued = 0;  // tiles whose loads were issued
       for (int j = 0; j < nkv; ++j) {
         const int ls = j % NS_LD, ks = j % NS_KV;
-        if (j >= NS_LD && !mbar_wait(&bars[bLdEmpty + pv * NS_LD + ls], ((j / NS_LD) - 1) & 1, abort, &g_attn_status))
+        if (!pv && j == a.stall_tile) break;  // abort test: tile j never arrives
+        if (j >= NS_LD &&
+            !mbar_wait(&bars[bLdEmpty + pv * NS_LD + ls], ((j / NS_LD) - 1) & 1, abort, &g_attn_status, lim))
           break;
         const int64_t t0 = a.lo + static_cast<int64_t>(j) * BN;
         const int64_t t1 = a.lo + min(static_cast<int64_t>(j + 1) * BN, static_cast<int64_t>(a.Lk));
         const bool has_sink = t0 < a.sink_tokens;
         const bool has_codes = t1 > a.sink_tokens;
         if (has_sink && j >= NS_KV &&
-            !mbar_wait(&bars[bKvEmpty + pv * NS_KV + ks], ((j / NS_KV) - 1) & 1, abort, &g_attn_status))
+            !mbar_wait(&bars[bKvEmpty + pv * NS_KV + ks], ((j / NS_KV) - 1) & 1, abort, &g_attn_status, lim))
           break;
         const uint32_t bytes = (has_codes ? code_tile : 0u) + (has_sink ? static_cast<uint32_t>(kKVTile) : 0u);
         uint64_t* full = &bars[bLdFull + pv * NS_LD + ls];
@@ -678,7 +695,16 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
           tma_load_2d(d, tsk, h * D, row, full);
           tma_load_2d(d + kAtom, tsk, h * D + 64, row, full);
         }
+        issued = j + 1;
       }
+      // Leave no copy into this CTA's shared memory in flight, also when another
+      // thread gave up before consuming it: wait for the last NS_LD tiles issued
+      // (each on its own stage, so each parity names one phase) and for the Q
+      // tiles. Without an abort they have landed long ago.
+      for (int j = max(0, issued - NS_LD); j < issued; ++j)
+        mbar_drain(&bars[bLdFull + pv * NS_LD + j % NS_LD], (j / NS_LD) & 1, &g_attn_status, lim);
+      if (!pv)
+        for (int x = 0; x < nq; ++x) mbar_drain(&bars[bQReady + x], 0, &g_attn_status, lim);
     }
     __syncwarp();
   } else if (warp == kMmaWarp || warp == kMmaWarp + 1) {
@@ -708,9 +734,9 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
                       (j > 0 || kk > 0) ? 1u : 0u);
       };
       auto wait_kv = [&](int j) {
-        return mbar_wait(&bars[bKvFull + j % NS_KV], (j / NS_KV) & 1, abort, &g_attn_status);
+        return mbar_wait(&bars[bKvFull + j % NS_KV], (j / NS_KV) & 1, abort, &g_attn_status, lim);
       };
-      bool ok = mbar_wait(&bars[bQReady + x], 0, abort, &g_attn_status) && wait_kv(0);
+      bool ok = mbar_wait(&bars[bQReady + x], 0, abort, &g_attn_status, lim) && wait_kv(0);
       if (ok) {
         tc_fence_after();
         issue_s(0);
@@ -723,9 +749,10 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
         // V(j) and K(j+2) were converted tiles ago (their stages came free at
         // S(j-2)): confirm them before waiting for P_x(j), off the chain
         // P_x(j) -> PV_x(j) -> S_x(j+2)
-        if (!(ok = mbar_wait(&bars[bKvFull + NS_KV + j % NS_KV], (j / NS_KV) & 1, abort, &g_attn_status))) break;
+        if (!(ok = mbar_wait(&bars[bKvFull + NS_KV + j % NS_KV], (j / NS_KV) & 1, abort, &g_attn_status, lim)))
+          break;
         if (j + 2 < nkv && !(ok = wait_kv(j + 2))) break;
-        if (!(ok = mbar_wait(&bars[bPFull + 2 * x + (j & 1)], (j >> 1) & 1, abort, &g_attn_status))) break;
+        if (!(ok = mbar_wait(&bars[bPFull + 2 * x + (j & 1)], (j >> 1) & 1, abort, &g_attn_status, lim))) break;
         tc_fence_after();
         issue_pv(j);
         if (j + 2 < nkv) {
@@ -738,7 +765,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
       if (ok) mma_commit(&bars[bOFinal + x]);
       // all MMAs issued by this thread have completed before TMEM is released
       mma_commit(&bars[bMmaDone + x]);
-      mbar_wait(&bars[bMmaDone + x], 0, abort, &g_attn_status);
+      mbar_drain(&bars[bMmaDone + x], 0, &g_attn_status, lim);
     }
     __syncwarp();
   }
@@ -838,7 +865,9 @@ static int attention_impl(const void* q, int64_t q_token_stride, const void* k_c
                           int64_t cache_tokens, int64_t sink_tokens, int64_t lo, int64_t hi, void* const* outs,
                           int n_outs, int out_head0, int out_heads, int64_t out_token_stride, int batch, int64_t n_q,
                           int n_heads, int head_dim, const int32_t* chan_band, int n_groups, int k_bits, int v_bits,
-                          float softmax_scale, void* stream, bool tma_out, float* stats) {
+                          float softmax_scale, void* stream, bool tma_out, float* stats,
+                          long long wait_cycles = sm100::kWaitCycles, int stall_tile = -1,
+                          unsigned* const* signals = nullptr) {
   KVQ_REQUIRE(head_dim == 128, KVQ_ERR_UNSUPPORTED, "attention supports head_dim 128, got %d", head_dim);
   KVQ_REQUIRE((k_bits == 4 || k_bits == 8) && v_bits == 4, KVQ_ERR_UNSUPPORTED,
               "attention reads int4 or int8 K and int4 V (got %d/%d bits)",
@@ -917,6 +946,13 @@ static int attention_impl(const void* q, int64_t q_token_stride, const void* k_c
   a.Lq = static_cast<int>(n_q);
   a.H = n_heads;
   for (int d = 0; d < n_outs; ++d) a.out[d] = static_cast<uint16_t*>(outs[d]);
+  if (signals) {
+    for (int d = 0; d < n_outs; ++d) {
+      KVQ_REQUIRE(signals[d] && (reinterpret_cast<uintptr_t>(signals[d]) & 3) == 0, KVQ_ERR_ARG,
+                  "signal counter %d is NULL or not 4-byte aligned", d);
+      a.sig[d] = signals[d];
+    }
+  }
   a.tma_out = tma_out ? 1 : 0;
   KVQ_REQUIRE(stats == nullptr || (reinterpret_cast<uintptr_t>(stats) & 15) == 0, KVQ_ERR_ALIGN,
               "stats must be 16-byte aligned");
@@ -935,6 +971,8 @@ static int attention_impl(const void* q, int64_t q_token_stride, const void* k_c
   a.o_batch_stride = out_token_stride * n_q;
   const float sc = softmax_scale > 0.0f ? softmax_scale : 1.0f / sqrtf(static_cast<float>(head_dim));
   a.scale_log2 = sc * 1.4426950408889634f;
+  a.wait_cycles = wait_cycles;
+  a.stall_tile = stall_tile;
   const int ctas = static_cast<int>((n_q + 2 * attn::BM - 1) / (2 * attn::BM));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   switch (layout) {
@@ -989,14 +1027,63 @@ extern "C" int kvq_attention_stats(const void* q, int64_t q_token_stride, const 
 extern "C" int kvq_attention_gather(const void* q, int64_t q_token_stride, const void* k_codes,
                                     const void* k_scales, const void* k_sink, const void* v_codes,
                                     const void* v_scales, const void* v_sink, int64_t cache_tokens,
-                                    int64_t sink_tokens, int64_t lo, int64_t hi, void* const* outs, int n_outs,
-                                    int out_head0, int out_heads, int64_t out_token_stride, int batch, int64_t n_q,
-                                    int n_heads, int head_dim, const int32_t* chan_band, int n_groups, int k_bits,
-                                    int v_bits, float softmax_scale, void* stream) {
+                                    int64_t sink_tokens, int64_t lo, int64_t hi, void* const* outs,
+                                    unsigned int* const* signals, int n_outs, int out_head0, int out_heads,
+                                    int64_t out_token_stride, int batch, int64_t n_q, int n_heads, int head_dim,
+                                    const int32_t* chan_band, int n_groups, int k_bits, int v_bits,
+                                    float softmax_scale, void* stream) {
   clear_error();
   return attention_impl(q, q_token_stride, k_codes, k_scales, k_sink, v_codes, v_scales, v_sink, cache_tokens,
                         sink_tokens, lo, hi, outs, n_outs, out_head0, out_heads, out_token_stride, batch, n_q,
-                        n_heads, head_dim, chan_band, n_groups, k_bits, v_bits, softmax_scale, stream, true, nullptr);
+                        n_heads, head_dim, chan_band, n_groups, k_bits, v_bits, softmax_scale, stream, true, nullptr,
+                        sm100::kWaitCycles, -1, signals);
+}
+
+namespace kvq {
+// One thread waits until the counter reaches `target` (wrap-around safe), then
+// returns; gives up after `limit` cycles and raises the device status word.
+__global__ void gather_wait_kernel(const unsigned* counter, unsigned target, long long limit) {
+  const long long t0 = clock64();
+  while (static_cast<int>(sm100::ld_acquire_sys(counter) - target) < 0) {
+    if (clock64() - t0 > limit) {
+      atomicExch(&g_attn_status, sm100::kDevTimeout);
+      return;
+    }
+    __nanosleep(256);
+  }
+  sm100::fence_proxy_async_global();
+}
+}  // namespace kvq
+
+extern "C" int kvq_gather_wait(const unsigned int* counter, unsigned int target, int64_t wait_cycles, void* stream) {
+  clear_error();
+  KVQ_REQUIRE(counter && (reinterpret_cast<uintptr_t>(counter) & 3) == 0, KVQ_ERR_ARG,
+              "counter is NULL or not 4-byte aligned");
+  KVQ_REQUIRE(wait_cycles >= 1000 && wait_cycles <= sm100::kWaitCycles, KVQ_ERR_ARG,
+              "wait_cycles must lie in [1000, %lld]", (long long)sm100::kWaitCycles);
+  int rc = require_sm100();
+  if (rc) return rc;
+  kvq::gather_wait_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(counter, target, wait_cycles);
+  return check_launch("kvq_gather_wait");
+}
+
+extern "C" int kvq_test_attention_timeout(const void* q, int64_t q_token_stride, const void* k_codes,
+                                          const void* k_scales, const void* k_sink, const void* v_codes,
+                                          const void* v_scales, const void* v_sink, int64_t cache_tokens,
+                                          int64_t sink_tokens, int64_t lo, int64_t hi, void* out,
+                                          int64_t out_token_stride, int batch, int64_t n_q, int n_heads, int head_dim,
+                                          const int32_t* chan_band, int n_groups, int k_bits, int v_bits,
+                                          float softmax_scale, int stall_tile, int64_t wait_cycles, void* stream) {
+  clear_error();
+  KVQ_REQUIRE(stall_tile >= 0, KVQ_ERR_ARG, "stall_tile must be >= 0");
+  KVQ_REQUIRE(wait_cycles >= 1000 && wait_cycles <= sm100::kWaitCycles, KVQ_ERR_ARG,
+              "wait_cycles must lie in [1000, %lld]", (long long)sm100::kWaitCycles);
+  void* outs[1] = {out};
+  KVQ_REQUIRE(n_q > 0 && out, KVQ_ERR_ARG, "NULL output or no queries");
+  return attention_impl(q, q_token_stride, k_codes, k_scales, k_sink, v_codes, v_scales, v_sink, cache_tokens,
+                        sink_tokens, lo, hi, outs, 1, 0, n_heads, out_token_stride, batch, n_q, n_heads, head_dim,
+                        chan_band, n_groups, k_bits, v_bits, softmax_scale, stream, true, nullptr, wait_cycles,
+                        stall_tile);
 }
 
 extern "C" int kvq_device_status(int reset) {

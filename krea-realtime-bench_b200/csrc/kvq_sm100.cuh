@@ -58,17 +58,18 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parit
 }
 
 // Waits until the phase with the given parity of `bar` has completed. Gives up
-// after about a second, or at once when another thread already gave up
-// (*abort != 0); on giving up it raises *abort and the device status word.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                          int* status) {
+// after `limit` cycles (kWaitCycles, about a second, unless a caller asks for
+// less), or at once when another thread already gave up (*abort != 0); on giving
+// up it raises *abort and the device status word.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* status,
+                                          long long limit = kWaitCycles) {
   const uint32_t b = smem_u32(bar);
   if (mbar_try_wait(b, parity)) return true;
   const long long t0 = clock64();
   while (true) {
     if (mbar_try_wait_sleep(b, parity)) return true;
     if (*abort) return false;
-    if (clock64() - t0 > kWaitCycles) {
+    if (clock64() - t0 > limit) {
       *abort = 1;
       atomicExch(status, kDevTimeout);
       return false;
@@ -76,11 +77,28 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// Waits for a phase that is bound to complete (an issued TMA copy landing, issued
+// MMAs finishing) even after another thread gave up: the abort path uses it so
+// that no copy into shared memory and no MMA on TMEM is still in flight when the
+// CTA releases them. Gives up after `limit` cycles all the same.
+__device__ __forceinline__ bool mbar_drain(uint64_t* bar, uint32_t parity, int* status,
+                                           long long limit = kWaitCycles) {
+  const uint32_t b = smem_u32(bar);
+  const long long t0 = clock64();
+  while (!mbar_try_wait(b, parity)) {
+    if (clock64() - t0 > limit) {
+      atomicExch(status, kDevTimeout);
+      return false;
+    }
+  }
+  return true;
+}
+
 // Warp-uniform wait: lane 0 waits, the result is broadcast to the warp.
-__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                               int* status) {
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort, int* status,
+                                               long long limit = kWaitCycles) {
   int ok = 0;
-  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort, status) ? 1 : 0;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort, status, limit) ? 1 : 0;
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
@@ -120,6 +138,24 @@ __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.comm
 // Waits until the committed bulk stores have finished reading shared memory.
 __device__ __forceinline__ void bulk_wait_read_all() {
   asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// Waits until the committed bulk stores have completed (their writes performed).
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Orders this thread's completed async-proxy (TMA) global writes before its later
+// generic-proxy operations.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+// Adds v to a 32-bit counter in global memory (possibly a peer GPU's, mapped over
+// NVLink) with release semantics at system scope: writes this thread performed or
+// observed before it are visible to whoever acquires the new value.
+__device__ __forceinline__ void red_release_sys_add(unsigned* p, unsigned v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");

@@ -239,14 +239,39 @@ def attention_packed(q: torch.Tensor, k_cache, v_cache, lo: int, hi: int, out: t
     return out
 
 
+def attention_timeout_test(q: torch.Tensor, k_cache, v_cache, lo: int, hi: int, stall_tile: int,
+                           wait_cycles: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    """attention_packed() with the K tiles from `stall_tile` on withheld and every
+    bounded wait limited to `wait_cycles` (kvq_test_attention_timeout): the
+    launch gives up, raises the device status word and returns; its output is
+    invalid. A test hook of the abort path, not a compute entry point."""
+    dev = _require_cuda(q, k_cache.packed, v_cache.packed, out)
+    B, Lq, H, D = q.shape
+    q = q.contiguous()
+    if out is None:
+        out = torch.empty((B, Lq, H, D), dtype=torch.bfloat16, device=dev)
+    cb = _host_map(k_cache.chan_band_host)
+    with torch.cuda.device(dev):
+        rc = _lib.load().kvq_test_attention_timeout(
+            _ptr(q), q.stride(1), _ptr(k_cache.packed), _ptr(k_cache.scales), _ptr(k_cache.sink),
+            _ptr(v_cache.packed), _ptr(v_cache.scales), _ptr(v_cache.sink), k_cache.n_tokens,
+            k_cache.sink_tokens if k_cache.sink is not None else 0, int(lo), int(hi), _ptr(out), out.stride(1),
+            B, Lq, H, D, cb.ctypes.data_as(ctypes.c_void_p), len(k_cache.bands), k_cache.bits, v_cache.bits, 0.0,
+            int(stall_tile), int(wait_cycles), _stream(dev))
+    _lib.check(rc, "kvq_test_attention_timeout")
+    return out
+
+
 def attention_packed_gather(q: torch.Tensor, k_cache, v_cache, lo: int, hi: int, outs: list[int],
                             out_head0: int, out_heads: int, out_token_stride: int | None = None,
-                            softmax_scale: float | None = None) -> None:
+                            softmax_scale: float | None = None, signals: list[int] | None = None) -> None:
     """Head-sharded attention whose epilogue is the output all-gather: the H heads
     of q [B, Lq, H, D] (heads out_head0.. of the full model) are written into each
     of the device buffers `outs` (raw pointers, e.g. PeerOutputs.ptrs: this GPU's
     and its peers'), all laid out [B, Lq, out_heads, D] bf16 with the given token
-    stride (default out_heads * D)."""
+    stride (default out_heads * D). With `signals` (one 32-bit counter per
+    destination, e.g. PeerOutputs.sig_ptrs), every stored 128-row tile adds 1 to
+    each destination's counter once its rows have landed (see gather_wait)."""
     dev = _require_cuda(q, k_cache.packed, v_cache.packed)
     if q.dtype != torch.bfloat16 or q.dim() != 4:
         raise TypeError("q must be a [B, Lq, H, D] bfloat16 tensor")
@@ -263,16 +288,38 @@ def attention_packed_gather(q: torch.Tensor, k_cache, v_cache, lo: int, hi: int,
         q = q.contiguous()
     stride = out_heads * D if out_token_stride is None else int(out_token_stride)
     arr = (ctypes.c_void_p * len(outs))(*[ctypes.c_void_p(int(p)) for p in outs])
+    if signals is not None and len(signals) != len(outs):
+        raise ValueError("one signal counter per output buffer")
+    sig = (ctypes.c_void_p * len(outs))(*[ctypes.c_void_p(int(p)) for p in signals]) if signals is not None else None
     cb = _host_map(k_cache.chan_band_host)
     with torch.cuda.device(dev):
         rc = _lib.load().kvq_attention_gather(
             _ptr(q), q.stride(1), _ptr(k_cache.packed), _ptr(k_cache.scales), _ptr(k_cache.sink),
             _ptr(v_cache.packed), _ptr(v_cache.scales), _ptr(v_cache.sink), k_cache.n_tokens,
             k_cache.sink_tokens if k_cache.sink is not None else 0, int(lo), int(hi),
-            ctypes.cast(arr, ctypes.c_void_p), len(outs), int(out_head0), int(out_heads), stride,
+            ctypes.cast(arr, ctypes.c_void_p), ctypes.cast(sig, ctypes.c_void_p) if sig is not None else None,
+            len(outs), int(out_head0), int(out_heads), stride,
             B, Lq, H, D, cb.ctypes.data_as(ctypes.c_void_p), len(k_cache.bands), k_cache.bits, v_cache.bits,
             float(softmax_scale) if softmax_scale else 0.0, _stream(dev))
     _lib.check(rc, "kvq_attention_gather")
+
+
+def gather_tiles(batch: int, n_q: int, n_heads: int) -> int:
+    """What one attention_packed_gather launch adds to each destination counter:
+    its 128-row output tiles, batch * n_heads * ceil(n_q / 128)."""
+    return batch * n_heads * ((n_q + 127) // 128)
+
+
+def gather_wait(counter: torch.Tensor, target: int, wait_cycles: int = 2_000_000_000) -> None:
+    """Makes the current stream wait (on the device, one thread) until this GPU's
+    signal counter (int32 tensor element, e.g. PeerOutputs.signal) reaches
+    `target` modulo 2^32; gives up after wait_cycles and raises the device status
+    word instead of hanging (kvq_gather_wait)."""
+    dev = _require_cuda(counter)
+    with torch.cuda.device(dev):
+        rc = _lib.load().kvq_gather_wait(_ptr(counter), ctypes.c_uint(int(target) & 0xFFFFFFFF),
+                                         int(wait_cycles), _stream(dev))
+    _lib.check(rc, "kvq_gather_wait")
 
 
 def ipc_export(t: torch.Tensor) -> tuple[bytes, int]:

@@ -54,15 +54,29 @@ def assemble_heads(gathered: torch.Tensor) -> torch.Tensor:
 class PeerOutputs:
     """A full-width output buffer [B, Lq, H, D] bf16 on every rank, mapped into
     every other rank (CUDA IPC), for ops.attention_packed_gather(). `ptrs` lists
-    the buffers rank by rank, this rank's own first-hand pointer included; after
-    every rank's gather launch of a step has completed (e.g. a barrier after the
-    synchronize), `local` holds the whole step's output on every rank.
+    the buffers rank by rank, this rank's own first-hand pointer included.
+
+    Completion without a host barrier: `signal` is a 32-bit counter in this
+    rank's memory and `sig_ptrs` lists every rank's counter (mapped like the
+    buffers). Pass `sig_ptrs` as the gather's signals; every output tile that
+    lands adds 1 to each rank's counter. `expect(n_tiles)` advances this rank's
+    target by the tiles all ranks store in one step (ops.gather_tiles summed over
+    the ranks) and `wait()` makes the current stream wait for it on the device;
+    afterwards `local` holds the whole step's output. Without signals, order the
+    step by kernel completion instead: a stream synchronize on every rank, then a
+    barrier.
+
+    Reuse: a rank may store into the buffers again only once every rank has
+    finished reading the previous step's `local`. Alternate two PeerOutputs (a
+    rank that passed wait() for step s knows every rank launched step s, and so
+    finished whatever it ordered before it, e.g. its reads of step s-1), or put a
+    barrier before the next launch.
 
     `exchange` is the collective that gathers one picklable object per rank
     (dist.all_gather_object by default); `ops` provides ipc_export / ipc_import /
     ipc_close (both replaceable for tests without GPUs)."""
 
-    def __init__(self, local: torch.Tensor, group=None, exchange=None, ops=None):
+    def __init__(self, local: torch.Tensor, group=None, exchange=None, ops=None, signals: bool = True):
         if ops is None:
             from . import ops as _ops
             ops = _ops
@@ -75,23 +89,45 @@ class PeerOutputs:
                 got = [None] * world
                 dist.all_gather_object(got, obj, group=group)
                 return got
-        mine = ops.ipc_export(local)
+        # the counter gets an allocation of its own (a page), so that its IPC
+        # mapping never aliases the output buffer's
+        self.signal = torch.zeros(64, dtype=torch.int32, device=local.device) if signals else None
+        self.target = 0
+        mine = (ops.ipc_export(local), ops.ipc_export(self.signal) if signals else None)
         got = exchange(mine)
         if len(got) != world:
             raise RuntimeError(f"exchange returned {len(got)} entries for {world} ranks")
         self.ptrs: list[int] = []
+        self.sig_ptrs: list[int] | None = [] if signals else None
         self._bases: list[int] = []
         try:
-            for r, (handle, offset) in enumerate(got):
+            for r, (buf, sig) in enumerate(got):
                 if r == rank:
                     self.ptrs.append(local.data_ptr())
-                else:
-                    base, ptr = ops.ipc_import(handle, offset)
+                    if signals:
+                        self.sig_ptrs.append(self.signal.data_ptr())
+                    continue
+                base, ptr = ops.ipc_import(*buf)
+                self._bases.append(base)
+                self.ptrs.append(ptr)
+                if signals:
+                    base, ptr = ops.ipc_import(*sig)
                     self._bases.append(base)
-                    self.ptrs.append(ptr)
+                    self.sig_ptrs.append(ptr)
         except Exception:
             self.close()
             raise
+
+    def expect(self, n_tiles: int) -> int:
+        """Advances the target by the output tiles all ranks store in one step."""
+        self.target = (self.target + int(n_tiles)) & 0xFFFFFFFF
+        return self.target
+
+    def wait(self, wait_cycles: int = 2_000_000_000) -> None:
+        """Current stream waits on the device until the target is reached."""
+        if self.signal is None:
+            raise RuntimeError("PeerOutputs made without signals")
+        self._ops.gather_wait(self.signal, self.target, wait_cycles)
 
     def close(self) -> None:
         """Unmaps the peers' buffers (call before the peers free theirs)."""

@@ -121,6 +121,8 @@ class QuantKVTensor:
         self.lossless_moves = bool(lossless_moves)
         self.chan_band = _kern.build_chan_band(self.bands, d, dev)
         self.chan_band_host = np.ascontiguousarray(_kern.host_chan_band(self.chan_band))
+        # bumped by every write; a window read before a write refuses to be used after it
+        self.version = 0
 
     # ------------------------------------------------------------------ tensor-like
     @property
@@ -137,6 +139,7 @@ class QuantKVTensor:
         return 4
 
     def zero_(self):
+        self.version += 1
         self.packed.zero_()
         self.scales.zero_()
         if self.sink is not None:
@@ -190,6 +193,7 @@ class QuantKVTensor:
         v = value.unsqueeze(0) if value.dim() == 3 else value
         assert v.dim() == 4 and v.shape[0] == self.n_streams and v.shape[1] == b - a
         v = v.to(device=self.device, dtype=self.dtype)
+        self.version += 1
         freqs = freqs.to(self.device).contiguous()
         positions = positions.to(device=self.device, dtype=torch.int32).contiguous()
         G = len(self.bands)
@@ -243,6 +247,7 @@ class QuantKVTensor:
         in the sink (exact where blk's rows came from its cache's sink)."""
         L = b - a
         ns = max(0, min(b, self.sink_tokens) - a) if self.sink is not None else 0
+        self.version += 1
         for i in range(self.n_streams):
             rows = self._rows(i, a, b)
             self.packed[rows].copy_(blk.packed[i * L:(i + 1) * L])
@@ -251,12 +256,13 @@ class QuantKVTensor:
                 self.sink[self._sink_rows(i, a, a + ns)].copy_(blk.read_rows(i, 0, ns))
 
     def clone(self):
-        raise RuntimeError("clone() on the whole cache is never called by the runtime")
+        raise RuntimeError("QuantKVTensor.clone(): the runtime only clones windows (t[:, a:b].clone()); "
+                           "copying a whole packed cache is not supported")
 
     def __repr__(self):
-        gb = self.storage_bytes() / 1e9
-        return (f"QuantKVTensor({tuple(self.logical_shape)}, int{self.bits}, "
-                f"{self.group_mode}, sink={self.sink_tokens}, {gb:.3f} GB)")
+        return (f"<QuantKVTensor {list(self.logical_shape)} int{self.bits} groups={self.group_mode} "
+                f"({len(self.bands)}) sink_tokens={self.sink_tokens} on {self.device}: "
+                f"{self.storage_bytes() / 2**30:.2f} GiB resident>")
 
 
 def attention_stats(q, k, v, softmax_scale=None):
@@ -271,6 +277,8 @@ def attention_stats(q, k, v, softmax_scale=None):
         raise TypeError("attention_stats() takes k and v as QuantKVTensor windows (t[:, lo:hi])")
     if (k.lo, k.hi) != (v.lo, v.hi):
         raise ValueError(f"k window [{k.lo},{k.hi}) and v window [{v.lo},{v.hi}) differ")
+    k.check_fresh()
+    v.check_fresh()
     B, Lq, H, _ = q.shape
     stats = torch.empty((B, Lq, H, 4), dtype=torch.float32, device=k.cache.device)
     out = _ops.attention_packed(q, k.cache, v.cache, k.lo, k.hi, softmax_scale=softmax_scale, stats=stats)
@@ -286,6 +294,7 @@ def _write_tensors(pairs, a, b):
     ns = max(0, min(b, c0.sink_tokens) - a) if c0.sink is not None else 0
     xs, codes, scales, sinks = [], [], [], []
     for cache, v in pairs:
+        cache.version += 1
         for i in range(cache.n_streams):
             x = v[i]
             if x.stride(2) != 1 or x.stride(1) != cache.head_dim or x.data_ptr() % 16 or x.stride(0) % 8:
@@ -356,10 +365,23 @@ class QuantKVWindow:
     window of the reference's __getitem__ (quant_kv.py:189-199), materialized on
     use: torch functions (via __torch_function__), tensor methods and
     attributes (delegated), arithmetic operators and `.clone()`.
+
+    One difference to the reference, whose __getitem__ returns a snapshot: the
+    window is read when it is used, not when it is taken. So that this can never
+    return newer data silently, a window refuses to be used (RuntimeError) once
+    its cache has been written after the window was taken; take the window
+    again, or `.clone()` it before the write to keep the old contents. The
+    runtime's three patterns (quant_kv.py:12-14) always use a window at once.
     """
 
     def __init__(self, cache: QuantKVTensor, lo: int, hi: int):
         self.cache, self.lo, self.hi = cache, lo, hi
+        self.version = cache.version
+
+    def check_fresh(self):
+        if self.cache.version != self.version:
+            raise RuntimeError(f"window [{self.lo}, {self.hi}) of {self.cache!r} was taken before a later write "
+                               "to the cache; take it again (or clone() it before writing)")
 
     @property
     def shape(self):
@@ -381,6 +403,7 @@ class QuantKVWindow:
         return 4
 
     def materialize(self) -> torch.Tensor:
+        self.check_fresh()
         return self.cache.read(self.lo, self.hi)
 
     def clone(self, *a, **kw):
@@ -388,6 +411,7 @@ class QuantKVWindow:
         # reference dequantizes here and requantizes on the write (quant_kv.py:217-218);
         # with lossless_moves the clone keeps the packed rows instead
         if self.cache.lossless_moves:
+            self.check_fresh()
             return PackedBlock(self.cache, self.lo, self.hi)
         return self.materialize()
 
@@ -519,17 +543,33 @@ def install(pipeline, k_bits=4, v_bits=4, group_mode="bands", sink_frames=0, ver
         pipeline.v_shape = shape
         pipeline.kv_cache1 = cache
         if verbose:
-            tot = sum(e["k"].storage_bytes() + e["v"].storage_bytes() for e in cache)
-            bf16 = 2 * len(cache) * shape[0] * shape[1] * shape[2] * shape[3] * 2
-            print(f"QuantKVCache: {cache[0]['k']}  |  {len(cache)} layers  "
-                  f"{tot / 1e9:.3f} GB vs {bf16 / 1e9:.3f} GB bf16  "
-                  f"(frees {(bf16 - tot) / 1e9:.3f} GB)", flush=True)
+            packed = sum(e["k"].storage_bytes() + e["v"].storage_bytes() for e in cache)
+            dense = 2 * len(cache) * shape[0] * shape[1] * shape[2] * shape[3] * 2
+            print(f"[quant_kv] {len(cache)} layers x (K int{k_bits}, V int{v_bits}), window {shape[1]} tokens, "
+                  f"groups {group_mode}, sink {sink_tokens}: {packed / 2**30:.2f} GiB packed, "
+                  f"{dense / 2**30:.2f} GiB as bf16", flush=True)
 
     pipeline._initialize_kv_cache = _initialize_kv_cache
     return orig
 
 
-def attention(q, k, v, *args, softmax_scale=None, out=None, **kwargs):
+# The upstream attention wrapper's optional arguments after (q, k, v), in its
+# positional order (Wan's flash-attention wrapper; un-vendored, the reference's
+# probe forwards them unchanged, probe_attention.py:101,122).
+_UPSTREAM_ARGS = ("q_lens", "k_lens", "dropout_p", "softmax_scale", "q_scale", "causal", "window_size",
+                  "deterministic", "dtype", "fa_version")
+
+
+def _check_lens(lens, n, name):
+    if lens is None:
+        return
+    vals = lens.tolist() if isinstance(lens, torch.Tensor) else list(lens)
+    if any(int(x) != n for x in vals):
+        raise NotImplementedError(f"{name} other than the full length {n} (variable-length batches) "
+                                  "is not supported by the fused int4-KV attention")
+
+
+def attention(q, k, v, *args, out=None, **kwargs):
     """Attention over a cache read, consuming the packed window directly.
 
     The runtime's read path `attention(q, kv_cache["k"][:, lo:hi],
@@ -537,8 +577,13 @@ def attention(q, k, v, *args, softmax_scale=None, out=None, **kwargs):
     QuantKVWindow views of the same token range. Non-causal softmax(q k^T *
     scale) v, scale 1/sqrt(D) by default, bf16 output [B, Lq, H, D]. Plain
     tensors for k or v raise TypeError: this build has no non-packed path.
-    Extra positional/keyword arguments of the upstream signature other than
-    softmax_scale are not supported and raise.
+
+    The upstream wrapper's optional arguments are accepted, positionally or by
+    name, when they leave this computation unchanged: q_lens / k_lens equal to
+    the full lengths (or None), dropout_p 0, softmax_scale (used), q_scale None,
+    causal False, window_size (-1, -1), deterministic (the kernel is), dtype
+    bf16, fa_version (ignored). Anything else raises NotImplementedError rather
+    than computing something different; unknown names raise TypeError.
     """
     if not isinstance(k, QuantKVWindow) or not isinstance(v, QuantKVWindow) \
             or isinstance(k, PackedBlock) or isinstance(v, PackedBlock):
@@ -546,6 +591,29 @@ def attention(q, k, v, *args, softmax_scale=None, out=None, **kwargs):
                         "plain tensors and clones have no packed form in the cache")
     if (k.lo, k.hi) != (v.lo, v.hi):
         raise ValueError(f"k window [{k.lo},{k.hi}) and v window [{v.lo},{v.hi}) differ")
-    if args or kwargs:
-        raise TypeError(f"unsupported attention arguments: {args} {sorted(kwargs)}")
-    return _ops.attention_packed(q, k.cache, v.cache, k.lo, k.hi, out=out, softmax_scale=softmax_scale)
+    if len(args) > len(_UPSTREAM_ARGS):
+        raise TypeError(f"attention() takes at most {3 + len(_UPSTREAM_ARGS)} positional arguments")
+    opts = dict(zip(_UPSTREAM_ARGS, args))
+    for name, val in kwargs.items():
+        if name not in _UPSTREAM_ARGS:
+            raise TypeError(f"attention() got an unexpected keyword argument {name!r}")
+        if name in opts:
+            raise TypeError(f"attention() got multiple values for argument {name!r}")
+        opts[name] = val
+    k.check_fresh()
+    v.check_fresh()
+    _check_lens(opts.get("q_lens"), q.shape[1], "q_lens")
+    _check_lens(opts.get("k_lens"), k.hi - k.lo, "k_lens")
+    if float(opts.get("dropout_p") or 0.0) != 0.0:
+        raise NotImplementedError("dropout is not supported by the fused int4-KV attention")
+    if opts.get("q_scale") is not None:
+        raise NotImplementedError("q_scale is not supported by the fused int4-KV attention")
+    if opts.get("causal", False):
+        raise NotImplementedError("the cache read is non-causal; causal=True is not supported")
+    ws = opts.get("window_size", (-1, -1))
+    if ws is not None and tuple(int(x) for x in ws) != (-1, -1):
+        raise NotImplementedError("local window_size is not supported by the fused int4-KV attention")
+    dt = opts.get("dtype", torch.bfloat16)
+    if dt is not None and dt != torch.bfloat16:
+        raise NotImplementedError(f"output dtype {dt} is not supported (bf16 only)")
+    return _ops.attention_packed(q, k.cache, v.cache, k.lo, k.hi, out=out, softmax_scale=opts.get("softmax_scale"))

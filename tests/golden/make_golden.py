@@ -1,7 +1,8 @@
 """Generates the golden fixtures under tests/golden/ from the REFERENCE itself.
 
-Run in a container where the reference checkout is present:
-    python tests/golden/make_golden.py [/path/to/krea-realtime-bench]
+Run in a container where the reference checkout is present, naming it by
+argument or by the environment variable KREA_REFERENCE:
+    python tests/golden/make_golden.py /path/to/krea-realtime-bench
 It imports the reference's quant_kv.py (torch path on CPU, use_kernels False)
 and records, for seeded inputs, the reference's codes, scales, dequantized
 windows (with the bf16 sink overlay) and the dequant-then-fp32-SDPA attention.
@@ -16,7 +17,9 @@ import numpy as np
 import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("KREA_REFERENCE", "")
+if not REF or not os.path.isfile(os.path.join(REF, "quant_kv.py")):
+    raise SystemExit("usage: make_golden.py /path/to/krea-realtime-bench (or set KREA_REFERENCE)")
 sys.path.insert(0, REF)
 import quant_kv as ref  # noqa: E402  (the reference module)
 

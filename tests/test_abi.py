@@ -34,7 +34,7 @@ def test_every_declared_symbol_is_exported(libkvq):
 
 
 def test_abi_version(libkvq):
-    assert libkvq.kvq_abi_version() == 2
+    assert libkvq.kvq_abi_version() == 3
 
 
 def _cb(bands=((0, 44), (44, 86), (86, 128))):

@@ -33,18 +33,24 @@ def _oracle_window(x_bits, bands, sink, lo, hi):
     return w
 
 
-def _oracle_attention(q_bits, kw, vw, scale=None):
-    """fp32 softmax attention per (stream, head) with torch on the CPU; q [B,Lq,H,D]."""
+def _oracle_attention(q_bits, kw, vw, scale=None, chunk=2048):
+    """fp32 softmax attention per (stream, head) with torch on the CPU; q [B,Lq,H,D].
+    Queries go in chunks (fp32 logits, softmax and products), so that windows of
+    32,760 tokens need neither the whole logit matrix in memory nor the slow path
+    of the CPU's fused attention."""
     q = torch.from_numpy(ko.bf16_to_f32(q_bits))
     k = torch.from_numpy(ko.bf16_to_f32(kw))
     v = torch.from_numpy(ko.bf16_to_f32(vw))
-    B = q.shape[0]
-    outs = []
+    B, Lq, H, D = q.shape
+    sc = 1.0 / math.sqrt(D) if scale is None else scale
+    out = torch.empty((B, H, Lq, D), dtype=torch.float32)
     for b in range(B):
-        o = torch.nn.functional.scaled_dot_product_attention(
-            q[b].transpose(0, 1), k[b].transpose(0, 1), v[b].transpose(0, 1), scale=scale)
-        outs.append(o.transpose(0, 1))
-    return torch.stack(outs).numpy()
+        kb, vb = k[b].transpose(0, 1), v[b].transpose(0, 1)          # [H, Lk, D]
+        qb = q[b].transpose(0, 1)                                     # [H, Lq, D]
+        for i in range(0, Lq, chunk):
+            s = torch.matmul(qb[:, i:i + chunk], kb.transpose(1, 2)) * sc
+            out[b, :, i:i + chunk] = torch.matmul(torch.softmax(s, dim=-1), vb)
+    return out.transpose(1, 2).contiguous().numpy()
 
 
 def _check(o_gpu, o_ref, what):
@@ -96,6 +102,21 @@ def test_golden_reference_attention(golden):
 def test_config1_full_size():
     """Q [1, 4680, 40, 128] over a 4680-token int4 window with a 1560-token sink."""
     err = _run_case(1, 4680, 40, 4680, 0, 4680, 1560)
+    assert err.mean() < 5e-4
+
+
+@pytest.mark.parametrize("B,S,H,Lq,sink", [
+    (1, 18720, 2, 18720, 1560),   # window 12, prefill: the window's queries over the window
+    (1, 32760, 2, 4680, 1560),    # window 21, denoise step: one block's queries over the window
+    (1, 32760, 1, 32760, 1560),   # window 21, prefill
+    (4, 32760, 1, 4680, 1560),    # window 21 with 4 streams (the head-sharded workload's shape)
+])
+def test_long_windows(B, S, H, Lq, sink):
+    """The window lengths the prefill and denoise timings use: 293 and 512 KV
+    tiles per row, where the online softmax's lazy rescale and the fp32 row sums
+    run longest (reference window read quant_kv.py:189-199 at S = 32,760,
+    quant_kv.py:238-241)."""
+    err = _run_case(B, S, H, Lq, 0, S, sink, seed=S + Lq + B)
     assert err.mean() < 5e-4
 
 

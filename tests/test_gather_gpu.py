@@ -39,6 +39,35 @@ def test_gather_two_local_destinations_match_attention():
     assert ops.device_status() == 0
 
 
+def test_gather_signals_count_tiles_and_wait_is_bounded():
+    """Each stored 128-row tile adds 1 to every destination's counter once its rows
+    have landed; a stream-ordered wait for that count passes, and a wait for one
+    more than will ever arrive gives up, raises the status word and returns."""
+    from kvq import ops, synth
+    B, S, H, Lq, sink = 2, 500, 3, 300, 100
+    tk, tv = _caches(B, S, H, sink, seed=4)
+    q = synth.make_q(B, Lq, H, seed=8, device="cuda")
+    ref = ops.attention_packed(q, tk, tv, 0, S)
+    bufs = [torch.zeros((B, Lq, H, 128), dtype=torch.bfloat16, device="cuda") for _ in range(2)]
+    sigs = [torch.zeros(64, dtype=torch.int32, device="cuda") for _ in range(2)]
+    tiles = ops.gather_tiles(B, Lq, H)
+    assert tiles == 2 * 3 * 3
+    for step in (1, 2):
+        ops.attention_packed_gather(q, tk, tv, 0, S, [b.data_ptr() for b in bufs], 0, H,
+                                    signals=[t.data_ptr() for t in sigs])
+        for t in sigs:
+            ops.gather_wait(t, step * tiles)
+        torch.cuda.synchronize()
+        assert [int(t[0]) for t in sigs] == [step * tiles] * 2
+        for b in bufs:
+            assert torch.equal(b, ref)
+    assert ops.device_status() == 0
+    ops.gather_wait(sigs[0], 2 * tiles + 1, wait_cycles=200_000)
+    torch.cuda.synchronize()
+    assert ops.device_status(reset=True) == 1
+    assert ops.device_status() == 0
+
+
 def test_gather_window_and_padded_token_stride():
     """A window [lo, hi) inside the sink border and an output token stride wider
     than heads * D."""
@@ -95,11 +124,21 @@ def _two_gpu_worker(rank, world, port, paths):
     q = synth.make_q(B, Lq, h1 - h0, seed=11 + h0, device=dev)
     full = torch.zeros((B, Lq, H, 128), dtype=torch.bfloat16, device=dev)
     po = shard.PeerOutputs(full)
-    ops.attention_packed_gather(q, tk, tv, 0, S, po.ptrs, h0, H)
-    torch.cuda.synchronize()
-    dist.barrier()
     ref = shard.assemble_heads(shard.gather_outputs(ops.attention_packed(q, tk, tv, 0, S)))
-    ok = torch.equal(full, ref) and ops.device_status() == 0
+    ok = True
+    for _step in range(3):
+        # completion by the device-side signal: no synchronize, no barrier between
+        # the launch and the read of the gathered rows
+        full.zero_()
+        torch.cuda.synchronize()
+        dist.barrier()                      # every rank cleared its buffer before anyone stores
+        ops.attention_packed_gather(q, tk, tv, 0, S, po.ptrs, h0, H, signals=po.sig_ptrs)
+        po.expect(world * ops.gather_tiles(B, Lq, h1 - h0))
+        po.wait(wait_cycles=200_000_000)
+        ok = ok and torch.equal(full, ref)
+        torch.cuda.synchronize()
+        dist.barrier()                      # every rank compared before the next step clears
+    ok = ok and ops.device_status() == 0
     dist.barrier()          # every peer is done with `full` before it is unmapped and freed
     po.close()
     dist.barrier()
@@ -120,4 +159,8 @@ def test_gather_two_gpus():
         p.start()
     for p in procs:
         p.join(timeout=300)
+    for p in procs:                 # a stuck worker must not keep holding its GPU
+        if p.is_alive():
+            p.kill()
+            p.join()
     assert [p.exitcode for p in procs] == [0, 0]

@@ -93,3 +93,52 @@ def test_window_behaves_like_tensor():
     assert torch.equal(w - m, torch.zeros_like(m))
     assert w.shape == m.shape and w.dtype == torch.bfloat16 and w.device == m.device
     assert torch.equal(w[:, 3], m[:, 3])
+
+
+def test_stale_window_refuses_use():
+    """A window is read when used, so once its cache was written after the window
+    was taken, using it raises instead of returning the newer data (the
+    reference's __getitem__ returns a snapshot); a clone taken before the write
+    keeps the old contents."""
+    import quant_kv
+    from kvq import synth
+    t = quant_kv.QuantKVTensor([1, 64, 2, 128], "cuda", group_mode="bands4", sink_tokens=8)
+    t[:, 0:64] = synth.make_v(64, 2, seed=1).cuda().unsqueeze(0)
+    w = t[:, 0:32]
+    snap = w.clone()
+    t[:, 16:48] = synth.make_v(32, 2, seed=2).cuda().unsqueeze(0)
+    with pytest.raises(RuntimeError, match="taken before a later write"):
+        w.materialize()
+    q = synth.make_q(1, 8, 2, seed=3).cuda()
+    with pytest.raises(RuntimeError):
+        quant_kv.attention(q, w, t[:, 0:32])
+    assert not torch.equal(t[:, 0:32].materialize(), snap)       # the cache did change, the clone did not
+
+
+def test_attention_accepts_neutral_upstream_arguments():
+    """The upstream wrapper's optional arguments that do not change the result are
+    accepted, positionally or by name; the others raise."""
+    import quant_kv
+    from kvq import synth
+    S, H = 256, 2
+    tk = quant_kv.QuantKVTensor([1, S, H, 128], "cuda", group_mode="bands4")
+    tv = quant_kv.QuantKVTensor([1, S, H, 128], "cuda", group_mode="bands4")
+    tk[:, 0:S] = synth.make_k(S, H, seed=4).cuda().unsqueeze(0)
+    tv[:, 0:S] = synth.make_v(S, H, seed=5).cuda().unsqueeze(0)
+    q = synth.make_q(1, 40, H, seed=6).cuda()
+    ref = quant_kv.attention(q, tk[:, 0:S], tv[:, 0:S])
+    same = [
+        quant_kv.attention(q, tk[:, 0:S], tv[:, 0:S], None, torch.tensor([S]), 0.0),
+        quant_kv.attention(q, tk[:, 0:S], tv[:, 0:S], q_lens=torch.tensor([40]), causal=False,
+                           window_size=(-1, -1), deterministic=True, dtype=torch.bfloat16, fa_version=3),
+    ]
+    for o in same:
+        assert torch.equal(o.view(torch.int16), ref.view(torch.int16))
+    scaled = quant_kv.attention(q, tk[:, 0:S], tv[:, 0:S], softmax_scale=0.1)
+    assert not torch.equal(scaled, ref)
+    for bad in ({"causal": True}, {"dropout_p": 0.1}, {"window_size": (64, 64)}, {"k_lens": torch.tensor([S - 1])},
+                {"q_scale": 2.0}, {"dtype": torch.float16}):
+        with pytest.raises(NotImplementedError):
+            quant_kv.attention(q, tk[:, 0:S], tv[:, 0:S], **bad)
+    with pytest.raises(TypeError):
+        quant_kv.attention(q, tk[:, 0:S], tv[:, 0:S], bogus=1)

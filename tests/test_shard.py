@@ -94,19 +94,23 @@ def test_dead_rank_is_an_error_not_a_hang():
 
 
 class _FakeIpc:
-    """Stands in for kvq.ops' CUDA IPC calls: a 'handle' names the exporting rank."""
+    """Stands in for kvq.ops' CUDA IPC calls: a 'handle' names the exporting rank
+    and the export's serial number (0 = output buffer, 1 = signal counter)."""
 
     def __init__(self, rank):
         self.rank = rank
+        self.serial = 0
         self.opened, self.closed = [], []
 
     def ipc_export(self, t):
-        return (b"rank%d" % self.rank).ljust(64, b"\0"), 16 * self.rank
+        h = (b"rank%d:%d" % (self.rank, self.serial)).ljust(64, b"\0")
+        self.serial += 1
+        return h, 16 * self.rank
 
     def ipc_import(self, handle, offset):
-        peer = int(handle.rstrip(b"\0")[4:])
+        peer, serial = (int(x) for x in handle.rstrip(b"\0")[4:].split(b":"))
         assert offset == 16 * peer
-        base = 1000 * (peer + 1)
+        base = 1000 * (peer + 1) + 100 * serial
         self.opened.append(base)
         return base, base + offset
 
@@ -126,7 +130,11 @@ def _peer_worker(rank, world, port, paths):
     local = torch.zeros(4)
     po = shard.PeerOutputs(local, ops=fake)
     want = [local.data_ptr() if r == rank else 1000 * (r + 1) + 16 * r for r in range(world)]
-    ok = po.ptrs == want and len(fake.opened) == world - 1
+    want_sig = [po.signal.data_ptr() if r == rank else 1000 * (r + 1) + 100 + 16 * r for r in range(world)]
+    ok = po.ptrs == want and po.sig_ptrs == want_sig and len(fake.opened) == 2 * (world - 1)
+    # the completion target advances by each step's tiles, modulo 2^32
+    po.target = 0xFFFFFFF0
+    ok = ok and po.expect(0x20) == 0x10 and po.expect(5) == 0x15
     po.close()
     po.close()  # idempotent
     ok = ok and sorted(fake.closed) == sorted(fake.opened)
