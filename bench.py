@@ -309,7 +309,6 @@ def run_ours(args):
             # a completion counter per rank (device-side signal, no host barrier)
             peers.append(shard.PeerOutputs(torch.empty((B, LQ, H_TOTAL, D), dtype=torch.bfloat16, device=dev)))
     gbuf = shard.gather_buffer(sets[0][3], world) if world > 1 else None
-    step_tiles = world * ops.gather_tiles(B, LQ, Hl)     # output tiles all ranks store per step
     torch.cuda.synchronize()
 
     def step(i, kev=None):
@@ -318,16 +317,15 @@ def run_ours(args):
             kev[0].record()
         if fused:
             po = peers[i % N_SETS]
-            ops.attention_packed_gather(q, tk, tv, 0, LK, po.ptrs, h0, H_TOTAL, signals=po.sig_ptrs)
+            ops.attention_packed_gather(q, tk, tv, 0, LK, po.ptrs, h0, H_TOTAL)
         else:
             ops.attention_packed(q, tk, tv, 0, LK, out=out)
         if kev is not None:
             kev[1].record()
         if fused:
-            # the step's consumer may read po.local once every rank's tiles have landed:
-            # a stream-ordered wait on this GPU's counter (part of the timed step)
-            po.expect(step_tiles)
-            po.wait()
+            # the step's consumer may read po.local once every rank's launch has
+            # completed: a device-side barrier of the ranks (part of the timed step)
+            po.barrier()
         elif world > 1:
             shard.gather_outputs(out, gbuf)
 
@@ -470,7 +468,6 @@ def run_e2e(args, dev, world, B, Hl, h0, gbuf):
                for _ in range(no)]
         res = [p.local[rank] for p in pos]              # [LQ, 40, D]: the stream this rank serves
     oh = [torch.empty(res[0].shape, dtype=torch.bfloat16).pin_memory() for _ in range(no)]
-    step_tiles = world * ops.gather_tiles(B, LQ, Hl)
     s_up, s_cmp, s_dn = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     ev = lambda: torch.cuda.Event()  # noqa: E731
     up_done, cmp_done, dn_done = {}, {}, {}
@@ -495,9 +492,8 @@ def run_e2e(args, dev, world, B, Hl, h0, gbuf):
                 quant_kv.attention(qd[j], tk[:, 0:LK], tv[:, 0:LK], out=od[o])
             else:
                 po = pos[o]
-                ops.attention_packed_gather(qd[j], tk, tv, 0, LK, po.ptrs, h0, H_TOTAL, signals=po.sig_ptrs)
-                po.expect(step_tiles)
-                po.wait()
+                ops.attention_packed_gather(qd[j], tk, tv, 0, LK, po.ptrs, h0, H_TOTAL)
+                po.barrier()
             cmp_done[i] = ev()
             cmp_done[i].record(s_cmp)
         with torch.cuda.stream(s_dn):
@@ -810,7 +806,6 @@ def run_config4(args, dev, world, rank, peaks):
     else:
         pos = [shard.PeerOutputs(torch.empty((B, NB, H_TOTAL, D), dtype=torch.bfloat16, device=dev))
                for _ in range(2)]
-    step_tiles = world * ops.gather_tiles(B, NB, Hl)
     torch.cuda.synchronize()
 
     def block():
@@ -821,9 +816,8 @@ def run_config4(args, dev, world, rank, peaks):
                 ops.attention_packed(qs[layer], ck, cv, 0, S, out=outs[layer % 2])
             else:
                 po = pos[layer % 2]
-                ops.attention_packed_gather(qs[layer], ck, cv, 0, S, po.ptrs, h0, H_TOTAL, signals=po.sig_ptrs)
-                po.expect(step_tiles)
-                po.wait()
+                ops.attention_packed_gather(qs[layer], ck, cv, 0, S, po.ptrs, h0, H_TOTAL)
+                po.barrier()
 
     n_blocks = 2
     block()                                   # warm-up

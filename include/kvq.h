@@ -179,12 +179,8 @@ KVQ_API int kvq_rebuild_layers(int n_tensors, const void* const* x, int64_t x_to
  * With outs = every rank's output buffer (peers mapped by kvq_ipc_import()),
  * the epilogue is the all-gather of the output over NVLink: when every rank's
  * launch has completed, every rank holds the full [batch, n_q, out_heads, D].
- * signals: NULL, or n_outs counters (unsigned 32-bit, 4-byte aligned), signals[d]
- * in the memory of destination d (peers mapped like the outputs): every 128-row
- * output tile, once its stores have landed in all destinations, adds 1 to each
- * destination's counter with release semantics at system scope. A launch adds
- * batch * n_heads * ceil(n_q / 128) to each counter; a consumer waits with
- * kvq_gather_wait() for the sum over all ranks' launches of a step.
+ * To read the gathered output without a host barrier, follow the launch on
+ * every rank by kvq_gather_barrier() on the same stream.
  * Other arguments and errors as kvq_attention(). No counterpart in the
  * reference (single GPU); replaces the attention + NCCL all-gather pair of a
  * head-sharded deployment.
@@ -193,22 +189,26 @@ KVQ_API int kvq_attention_gather(const void* q, int64_t q_token_stride,
                                  const void* k_codes, const void* k_scales, const void* k_sink,
                                  const void* v_codes, const void* v_scales, const void* v_sink,
                                  int64_t cache_tokens, int64_t sink_tokens, int64_t lo, int64_t hi,
-                                 void* const* outs, unsigned int* const* signals, int n_outs,
-                                 int out_head0, int out_heads,
+                                 void* const* outs, int n_outs, int out_head0, int out_heads,
                                  int64_t out_token_stride, int batch, int64_t n_q,
                                  int n_heads, int head_dim, const int32_t* chan_band, int n_groups,
                                  int k_bits, int v_bits, float softmax_scale, void* stream);
 
 /*
- * Stream-ordered wait for a gather's completion: one thread on `stream` waits
- * until *counter (this GPU's signal counter of kvq_attention_gather()) reaches
- * target, compared modulo 2^32 (a difference below 2^31 counts as reached), so
- * that work launched after it on the stream reads the gathered output without a
- * host barrier. Gives up after wait_cycles (>= 1000, at most about a second),
- * raising the device status word (kvq_device_status()). No counterpart in the
- * reference (single GPU).
+ * Device-side barrier of the ranks of a head-sharded job, stream-ordered: one
+ * thread on `stream`, after the work before it on the stream (e.g. the rank's
+ * kvq_attention_gather()) has completed, adds 1 to every rank's counter
+ * counters[0..n_ranks) (unsigned 32-bit, 4-byte aligned, counters[self] in this
+ * GPU's memory, the others peers' counters mapped by kvq_ipc_import()) with
+ * release semantics at system scope, then waits until its own counter reaches
+ * target (compared modulo 2^32; target = n_ranks x the number of barriers so
+ * far) with acquire semantics. Work launched after it reads every rank's stores
+ * made before their barrier, without a host barrier. Gives up after wait_cycles
+ * (>= 1000, at most about a second), raising the device status word
+ * (kvq_device_status()). No counterpart in the reference (single GPU).
  */
-KVQ_API int kvq_gather_wait(const unsigned int* counter, unsigned int target, int64_t wait_cycles, void* stream);
+KVQ_API int kvq_gather_barrier(unsigned int* const* counters, int n_ranks, int self, unsigned int target,
+                               int64_t wait_cycles, void* stream);
 
 /*
  * CUDA IPC for the output buffers of kvq_attention_gather(). kvq_ipc_export()

@@ -129,7 +129,6 @@ struct alignas(64) Args {
   uint16_t* out[kMaxOut];  // n_out destinations of identical layout (this GPU's and peers')
   int n_out, out_head0;     // heads of this launch land at heads out_head0.. of each destination
   int tma_out;              // store through tm_out (one TMA store per Q tile and destination)
-  unsigned* sig[kMaxOut];   // or NULL: completion counter of destination d (in d's memory), +1 per Q tile stored
   float* stats;             // STATS kernels: [batch][n_q][n_heads][4] fp32 row statistics
   CUtensorMap tm_out[kMaxOut];  // destination d as [batch][n_q][out_heads * D] bf16, box 64 x 128 x 1, SWIZZLE_128B
   int64_t o_tok_stride, o_batch_stride;
@@ -541,17 +540,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
             tma_store_3d(&a.tm_out[d], stage + kQAtom, xq + 64, yq, b);
           }
           bulk_commit();
-          if (a.sig[0]) {
-            // completion signal of the gather: once this tile's stores have landed
-            // in every destination, add 1 to each destination's counter (release,
-            // system scope), so a consumer that acquires count >= its target reads
-            // every row without a host barrier
-            bulk_wait_all();
-            fence_proxy_async_global();
-            for (int d = 0; d < a.n_out; ++d) red_release_sys_add(a.sig[d], 1u);
-          } else {
-            bulk_wait_read_all();  // the staging buffer must outlive the reads
-          }
+          bulk_wait_read_all();  // the staging buffer must outlive the reads
         }
         __syncwarp();
       } else {
@@ -866,8 +855,7 @@ static int attention_impl(const void* q, int64_t q_token_stride, const void* k_c
                           int n_outs, int out_head0, int out_heads, int64_t out_token_stride, int batch, int64_t n_q,
                           int n_heads, int head_dim, const int32_t* chan_band, int n_groups, int k_bits, int v_bits,
                           float softmax_scale, void* stream, bool tma_out, float* stats,
-                          long long wait_cycles = sm100::kWaitCycles, int stall_tile = -1,
-                          unsigned* const* signals = nullptr) {
+                          long long wait_cycles = sm100::kWaitCycles, int stall_tile = -1) {
   KVQ_REQUIRE(head_dim == 128, KVQ_ERR_UNSUPPORTED, "attention supports head_dim 128, got %d", head_dim);
   KVQ_REQUIRE((k_bits == 4 || k_bits == 8) && v_bits == 4, KVQ_ERR_UNSUPPORTED,
               "attention reads int4 or int8 K and int4 V (got %d/%d bits)",
@@ -946,13 +934,6 @@ static int attention_impl(const void* q, int64_t q_token_stride, const void* k_c
   a.Lq = static_cast<int>(n_q);
   a.H = n_heads;
   for (int d = 0; d < n_outs; ++d) a.out[d] = static_cast<uint16_t*>(outs[d]);
-  if (signals) {
-    for (int d = 0; d < n_outs; ++d) {
-      KVQ_REQUIRE(signals[d] && (reinterpret_cast<uintptr_t>(signals[d]) & 3) == 0, KVQ_ERR_ARG,
-                  "signal counter %d is NULL or not 4-byte aligned", d);
-      a.sig[d] = signals[d];
-    }
-  }
   a.tma_out = tma_out ? 1 : 0;
   KVQ_REQUIRE(stats == nullptr || (reinterpret_cast<uintptr_t>(stats) & 15) == 0, KVQ_ERR_ALIGN,
               "stats must be 16-byte aligned");
@@ -1027,44 +1008,69 @@ extern "C" int kvq_attention_stats(const void* q, int64_t q_token_stride, const 
 extern "C" int kvq_attention_gather(const void* q, int64_t q_token_stride, const void* k_codes,
                                     const void* k_scales, const void* k_sink, const void* v_codes,
                                     const void* v_scales, const void* v_sink, int64_t cache_tokens,
-                                    int64_t sink_tokens, int64_t lo, int64_t hi, void* const* outs,
-                                    unsigned int* const* signals, int n_outs, int out_head0, int out_heads,
-                                    int64_t out_token_stride, int batch, int64_t n_q, int n_heads, int head_dim,
-                                    const int32_t* chan_band, int n_groups, int k_bits, int v_bits,
-                                    float softmax_scale, void* stream) {
+                                    int64_t sink_tokens, int64_t lo, int64_t hi, void* const* outs, int n_outs,
+                                    int out_head0, int out_heads, int64_t out_token_stride, int batch, int64_t n_q,
+                                    int n_heads, int head_dim, const int32_t* chan_band, int n_groups, int k_bits,
+                                    int v_bits, float softmax_scale, void* stream) {
   clear_error();
   return attention_impl(q, q_token_stride, k_codes, k_scales, k_sink, v_codes, v_scales, v_sink, cache_tokens,
                         sink_tokens, lo, hi, outs, n_outs, out_head0, out_heads, out_token_stride, batch, n_q,
-                        n_heads, head_dim, chan_band, n_groups, k_bits, v_bits, softmax_scale, stream, true, nullptr,
-                        sm100::kWaitCycles, -1, signals);
+                        n_heads, head_dim, chan_band, n_groups, k_bits, v_bits, softmax_scale, stream, true, nullptr);
 }
 
 namespace kvq {
-// One thread waits until the counter reaches `target` (wrap-around safe), then
-// returns; gives up after `limit` cycles and raises the device status word.
-__global__ void gather_wait_kernel(const unsigned* counter, unsigned target, long long limit) {
+constexpr int kMaxRanks = 64;
+struct BarrierArgs {
+  unsigned* counters[kMaxRanks];  // every rank's counter (this GPU's own and its peers', mapped)
+  int n, self;
+  unsigned target;
+  long long limit;
+};
+
+// One thread: every write of the kernels before this one on the stream has
+// completed (kernel boundary); release-add 1 to every rank's counter, then wait
+// (acquire) until this rank's counter reaches the target, i.e. until every rank
+// has passed the same point of its stream. Gives up after `limit` cycles and
+// raises the device status word instead of hanging.
+__global__ void gather_barrier_kernel(const __grid_constant__ BarrierArgs a) {
+  sm100::fence_proxy_async_global();
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+  for (int d = 0; d < a.n; ++d) sm100::red_release_sys_add(a.counters[d], 1u);
+  const unsigned* mine = a.counters[a.self];
   const long long t0 = clock64();
-  while (static_cast<int>(sm100::ld_acquire_sys(counter) - target) < 0) {
-    if (clock64() - t0 > limit) {
+  while (static_cast<int>(sm100::ld_acquire_sys(mine) - a.target) < 0) {
+    if (clock64() - t0 > a.limit) {
       atomicExch(&g_attn_status, sm100::kDevTimeout);
       return;
     }
-    __nanosleep(256);
+    __nanosleep(128);
   }
   sm100::fence_proxy_async_global();
 }
 }  // namespace kvq
 
-extern "C" int kvq_gather_wait(const unsigned int* counter, unsigned int target, int64_t wait_cycles, void* stream) {
+extern "C" int kvq_gather_barrier(unsigned int* const* counters, int n_ranks, int self, unsigned int target,
+                                  int64_t wait_cycles, void* stream) {
   clear_error();
-  KVQ_REQUIRE(counter && (reinterpret_cast<uintptr_t>(counter) & 3) == 0, KVQ_ERR_ARG,
-              "counter is NULL or not 4-byte aligned");
+  KVQ_REQUIRE(counters && n_ranks >= 1 && n_ranks <= kvq::kMaxRanks && self >= 0 && self < n_ranks, KVQ_ERR_ARG,
+              "1 to %d counters and 0 <= self < n_ranks", kvq::kMaxRanks);
   KVQ_REQUIRE(wait_cycles >= 1000 && wait_cycles <= sm100::kWaitCycles, KVQ_ERR_ARG,
               "wait_cycles must lie in [1000, %lld]", (long long)sm100::kWaitCycles);
+  kvq::BarrierArgs a;
+  memset(&a, 0, sizeof(a));
+  for (int d = 0; d < n_ranks; ++d) {
+    KVQ_REQUIRE(counters[d] && (reinterpret_cast<uintptr_t>(counters[d]) & 3) == 0, KVQ_ERR_ARG,
+                "counter %d is NULL or not 4-byte aligned", d);
+    a.counters[d] = counters[d];
+  }
+  a.n = n_ranks;
+  a.self = self;
+  a.target = target;
+  a.limit = wait_cycles;
   int rc = require_sm100();
   if (rc) return rc;
-  kvq::gather_wait_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(counter, target, wait_cycles);
-  return check_launch("kvq_gather_wait");
+  kvq::gather_barrier_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(a);
+  return check_launch("kvq_gather_barrier");
 }
 
 extern "C" int kvq_test_attention_timeout(const void* q, int64_t q_token_stride, const void* k_codes,

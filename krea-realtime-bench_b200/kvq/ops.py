@@ -264,14 +264,13 @@ def attention_timeout_test(q: torch.Tensor, k_cache, v_cache, lo: int, hi: int, 
 
 def attention_packed_gather(q: torch.Tensor, k_cache, v_cache, lo: int, hi: int, outs: list[int],
                             out_head0: int, out_heads: int, out_token_stride: int | None = None,
-                            softmax_scale: float | None = None, signals: list[int] | None = None) -> None:
+                            softmax_scale: float | None = None) -> None:
     """Head-sharded attention whose epilogue is the output all-gather: the H heads
     of q [B, Lq, H, D] (heads out_head0.. of the full model) are written into each
     of the device buffers `outs` (raw pointers, e.g. PeerOutputs.ptrs: this GPU's
     and its peers'), all laid out [B, Lq, out_heads, D] bf16 with the given token
-    stride (default out_heads * D). With `signals` (one 32-bit counter per
-    destination, e.g. PeerOutputs.sig_ptrs), every stored 128-row tile adds 1 to
-    each destination's counter once its rows have landed (see gather_wait)."""
+    stride (default out_heads * D). Every rank's buffer holds the whole output
+    once every rank has passed the following gather_barrier()."""
     dev = _require_cuda(q, k_cache.packed, v_cache.packed)
     if q.dtype != torch.bfloat16 or q.dim() != 4:
         raise TypeError("q must be a [B, Lq, H, D] bfloat16 tensor")
@@ -288,38 +287,30 @@ def attention_packed_gather(q: torch.Tensor, k_cache, v_cache, lo: int, hi: int,
         q = q.contiguous()
     stride = out_heads * D if out_token_stride is None else int(out_token_stride)
     arr = (ctypes.c_void_p * len(outs))(*[ctypes.c_void_p(int(p)) for p in outs])
-    if signals is not None and len(signals) != len(outs):
-        raise ValueError("one signal counter per output buffer")
-    sig = (ctypes.c_void_p * len(outs))(*[ctypes.c_void_p(int(p)) for p in signals]) if signals is not None else None
     cb = _host_map(k_cache.chan_band_host)
     with torch.cuda.device(dev):
         rc = _lib.load().kvq_attention_gather(
             _ptr(q), q.stride(1), _ptr(k_cache.packed), _ptr(k_cache.scales), _ptr(k_cache.sink),
             _ptr(v_cache.packed), _ptr(v_cache.scales), _ptr(v_cache.sink), k_cache.n_tokens,
             k_cache.sink_tokens if k_cache.sink is not None else 0, int(lo), int(hi),
-            ctypes.cast(arr, ctypes.c_void_p), ctypes.cast(sig, ctypes.c_void_p) if sig is not None else None,
-            len(outs), int(out_head0), int(out_heads), stride,
+            ctypes.cast(arr, ctypes.c_void_p), len(outs), int(out_head0), int(out_heads), stride,
             B, Lq, H, D, cb.ctypes.data_as(ctypes.c_void_p), len(k_cache.bands), k_cache.bits, v_cache.bits,
             float(softmax_scale) if softmax_scale else 0.0, _stream(dev))
     _lib.check(rc, "kvq_attention_gather")
 
 
-def gather_tiles(batch: int, n_q: int, n_heads: int) -> int:
-    """What one attention_packed_gather launch adds to each destination counter:
-    its 128-row output tiles, batch * n_heads * ceil(n_q / 128)."""
-    return batch * n_heads * ((n_q + 127) // 128)
-
-
-def gather_wait(counter: torch.Tensor, target: int, wait_cycles: int = 2_000_000_000) -> None:
-    """Makes the current stream wait (on the device, one thread) until this GPU's
-    signal counter (int32 tensor element, e.g. PeerOutputs.signal) reaches
-    `target` modulo 2^32; gives up after wait_cycles and raises the device status
-    word instead of hanging (kvq_gather_wait)."""
-    dev = _require_cuda(counter)
-    with torch.cuda.device(dev):
-        rc = _lib.load().kvq_gather_wait(_ptr(counter), ctypes.c_uint(int(target) & 0xFFFFFFFF),
-                                         int(wait_cycles), _stream(dev))
-    _lib.check(rc, "kvq_gather_wait")
+def gather_barrier(counters: list[int], self_index: int, target: int, wait_cycles: int = 2_000_000_000) -> None:
+    """Device-side barrier of the ranks on the current stream (kvq_gather_barrier):
+    adds 1 to every rank's counter (raw pointers, e.g. PeerOutputs.sig_ptrs) once
+    the work before it on the stream has completed, then waits on the device until
+    this rank's counter (counters[self_index]) reaches `target` modulo 2^32. Gives
+    up after wait_cycles and raises the device status word instead of hanging."""
+    n = len(counters)
+    arr = (ctypes.c_void_p * n)(*[ctypes.c_void_p(int(p)) for p in counters])
+    dev = torch.device("cuda", torch.cuda.current_device())
+    rc = _lib.load().kvq_gather_barrier(ctypes.cast(arr, ctypes.c_void_p), n, int(self_index),
+                                        ctypes.c_uint(int(target) & 0xFFFFFFFF), int(wait_cycles), _stream(dev))
+    _lib.check(rc, "kvq_gather_barrier")
 
 
 def ipc_export(t: torch.Tensor) -> tuple[bytes, int]:

@@ -58,19 +58,18 @@ class PeerOutputs:
 
     Completion without a host barrier: `signal` is a 32-bit counter in this
     rank's memory and `sig_ptrs` lists every rank's counter (mapped like the
-    buffers). Pass `sig_ptrs` as the gather's signals; every output tile that
-    lands adds 1 to each rank's counter. `expect(n_tiles)` advances this rank's
-    target by the tiles all ranks store in one step (ops.gather_tiles summed over
-    the ranks) and `wait()` makes the current stream wait for it on the device;
-    afterwards `local` holds the whole step's output. Without signals, order the
-    step by kernel completion instead: a stream synchronize on every rank, then a
-    barrier.
+    buffers). After each rank's gather launch of a step, `barrier()` on the same
+    stream (ops.gather_barrier) adds 1 to every rank's counter once the launch has
+    completed and waits on the device until all ranks have done so; work after it
+    on the stream reads the whole step's output from `local`. Without signals,
+    order the step on the host instead: a stream synchronize on every rank, then
+    a barrier.
 
     Reuse: a rank may store into the buffers again only once every rank has
     finished reading the previous step's `local`. Alternate two PeerOutputs (a
-    rank that passed wait() for step s knows every rank launched step s, and so
-    finished whatever it ordered before it, e.g. its reads of step s-1), or put a
-    barrier before the next launch.
+    rank that passed barrier() of step s knows that every rank finished the work
+    it ordered before its own step-s barrier, e.g. its reads of step s-1), or put
+    a barrier before the next launch.
 
     `exchange` is the collective that gathers one picklable object per rank
     (dist.all_gather_object by default); `ops` provides ipc_export / ipc_import /
@@ -93,6 +92,7 @@ class PeerOutputs:
         # mapping never aliases the output buffer's
         self.signal = torch.zeros(64, dtype=torch.int32, device=local.device) if signals else None
         self.target = 0
+        self.world, self.rank = world, rank
         mine = (ops.ipc_export(local), ops.ipc_export(self.signal) if signals else None)
         got = exchange(mine)
         if len(got) != world:
@@ -118,16 +118,16 @@ class PeerOutputs:
             self.close()
             raise
 
-    def expect(self, n_tiles: int) -> int:
-        """Advances the target by the output tiles all ranks store in one step."""
-        self.target = (self.target + int(n_tiles)) & 0xFFFFFFFF
+    def next_target(self) -> int:
+        """Advances this rank's barrier target by one barrier (one add per rank)."""
+        self.target = (self.target + self.world) & 0xFFFFFFFF
         return self.target
 
-    def wait(self, wait_cycles: int = 2_000_000_000) -> None:
-        """Current stream waits on the device until the target is reached."""
+    def barrier(self, wait_cycles: int = 2_000_000_000) -> None:
+        """Device-side barrier on the current stream (see the class docstring)."""
         if self.signal is None:
             raise RuntimeError("PeerOutputs made without signals")
-        self._ops.gather_wait(self.signal, self.target, wait_cycles)
+        self._ops.gather_barrier(self.sig_ptrs, self.rank, self.next_target(), wait_cycles)
 
     def close(self) -> None:
         """Unmaps the peers' buffers (call before the peers free theirs)."""

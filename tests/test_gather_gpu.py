@@ -39,30 +39,32 @@ def test_gather_two_local_destinations_match_attention():
     assert ops.device_status() == 0
 
 
-def test_gather_signals_count_tiles_and_wait_is_bounded():
-    """Each stored 128-row tile adds 1 to every destination's counter once its rows
-    have landed; a stream-ordered wait for that count passes, and a wait for one
-    more than will ever arrive gives up, raises the status word and returns."""
+def test_gather_barrier_counts_and_is_bounded():
+    """Two ranks emulated on one GPU, one stream, ordered so that no barrier waits
+    for a later launch: "rank 1" adds 1 to both counters and finds its own target
+    met, then "rank 0" adds 1 to both and finds its target met too; the gathered
+    rows are all there afterwards. A barrier whose target is never reached gives
+    up, raises the status word and returns."""
     from kvq import ops, synth
     B, S, H, Lq, sink = 2, 500, 3, 300, 100
     tk, tv = _caches(B, S, H, sink, seed=4)
     q = synth.make_q(B, Lq, H, seed=8, device="cuda")
     ref = ops.attention_packed(q, tk, tv, 0, S)
     bufs = [torch.zeros((B, Lq, H, 128), dtype=torch.bfloat16, device="cuda") for _ in range(2)]
-    sigs = [torch.zeros(64, dtype=torch.int32, device="cuda") for _ in range(2)]
-    tiles = ops.gather_tiles(B, Lq, H)
-    assert tiles == 2 * 3 * 3
+    ctr = torch.zeros(2 * 64, dtype=torch.int32, device="cuda")
+    ptrs = [ctr.data_ptr(), ctr.data_ptr() + 256]
     for step in (1, 2):
-        ops.attention_packed_gather(q, tk, tv, 0, S, [b.data_ptr() for b in bufs], 0, H,
-                                    signals=[t.data_ptr() for t in sigs])
-        for t in sigs:
-            ops.gather_wait(t, step * tiles)
+        ops.attention_packed_gather(q, tk, tv, 0, S, [b.data_ptr() for b in bufs], 0, H)
+        # "rank 1" signals first (it never waits long: its own target is reached by
+        # its own add plus rank 0's add of the previous step), then rank 0
+        ops.gather_barrier(ptrs, 1, 2 * step - 1)
+        ops.gather_barrier(ptrs, 0, 2 * step)
         torch.cuda.synchronize()
-        assert [int(t[0]) for t in sigs] == [step * tiles] * 2
+        assert int(ctr[0]) == 2 * step and int(ctr[64]) == 2 * step
         for b in bufs:
             assert torch.equal(b, ref)
     assert ops.device_status() == 0
-    ops.gather_wait(sigs[0], 2 * tiles + 1, wait_cycles=200_000)
+    ops.gather_barrier(ptrs, 0, 2 * 2 + 2, wait_cycles=200_000)   # only one more add will come
     torch.cuda.synchronize()
     assert ops.device_status(reset=True) == 1
     assert ops.device_status() == 0
@@ -132,9 +134,8 @@ def _two_gpu_worker(rank, world, port, paths):
         full.zero_()
         torch.cuda.synchronize()
         dist.barrier()                      # every rank cleared its buffer before anyone stores
-        ops.attention_packed_gather(q, tk, tv, 0, S, po.ptrs, h0, H, signals=po.sig_ptrs)
-        po.expect(world * ops.gather_tiles(B, Lq, h1 - h0))
-        po.wait(wait_cycles=200_000_000)
+        ops.attention_packed_gather(q, tk, tv, 0, S, po.ptrs, h0, H)
+        po.barrier(wait_cycles=200_000_000)
         ok = ok and torch.equal(full, ref)
         torch.cuda.synchronize()
         dist.barrier()                      # every rank compared before the next step clears

@@ -132,9 +132,9 @@ def _peer_worker(rank, world, port, paths):
     want = [local.data_ptr() if r == rank else 1000 * (r + 1) + 16 * r for r in range(world)]
     want_sig = [po.signal.data_ptr() if r == rank else 1000 * (r + 1) + 100 + 16 * r for r in range(world)]
     ok = po.ptrs == want and po.sig_ptrs == want_sig and len(fake.opened) == 2 * (world - 1)
-    # the completion target advances by each step's tiles, modulo 2^32
-    po.target = 0xFFFFFFF0
-    ok = ok and po.expect(0x20) == 0x10 and po.expect(5) == 0x15
+    # the barrier target advances by one add per rank, modulo 2^32
+    po.target = 0xFFFFFFFF - world + 2
+    ok = ok and po.next_target() == 1 and po.next_target() == 1 + world
     po.close()
     po.close()  # idempotent
     ok = ok and sorted(fake.closed) == sorted(fake.opened)
