@@ -548,6 +548,37 @@ def _time_events(fn, n, warm=2):
     return [a.elapsed_time(b) for a, b in ev]
 
 
+def _time_graph(fn, n, reps=5):
+    """Per-call device time of fn(i) for i < n launched back to back: the n calls
+    are captured in one CUDA graph, so host-side argument handling between the
+    launches is not timed (a small kernel timed call by call measures the host).
+    Returns per-call ms of each replay."""
+    fn(0)                                    # warm-up (one-time set-up happens outside the capture)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        fn(0)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g, stream=s):
+            for i in range(n):
+                fn(i)
+    torch.cuda.current_stream().wait_stream(s)
+    g.replay()
+    torch.cuda.synchronize()
+    out = []
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        out.append(e0.elapsed_time(e1) / n)
+    del g
+    return out
+
+
 def run_extras(dev, peaks):
     """Quantize/dequantize GB/s and prefill ms/block at windows 3/12/21."""
     import quant_kv
@@ -567,18 +598,19 @@ def run_extras(dev, peaks):
             for t in range(2):  # K and V of one layer
                 j = (2 * i + t) % 4
                 ops.quantize_into(xs[j], cs[j], ss[j], cb, G, 4)
-        ms = _time_events(fq, 20)
+        ms = _time_graph(fq, 20)
         byts = 2 * L * H_TOTAL * quant_bytes_per_row(G)
         gbs = byts / (statistics.median(ms) / 1e3) / 1e9
         res[f"quantize_{name}"] = {"gbs": gbs, "ms": statistics.median(ms), "bytes": byts,
-                                   "frac_hbm": gbs / peaks["hbm_gbs"]}
+                                   "frac_hbm": gbs / peaks["hbm_gbs"],
+                                   "timing": "CUDA graph of 20 iterations (K and V: two launches each)"}
         outs = [torch.empty_like(x) for x in xs]
 
         def fd(i):
             for t in range(2):
                 j = (2 * i + t) % 4
                 ops.dequantize_into(cs[j], ss[j], outs[j], cb, G, 4)
-        ms = _time_events(fd, 20)
+        ms = _time_graph(fd, 20)
         res[f"dequantize_{name}"] = {"gbs": byts / (statistics.median(ms) / 1e3) / 1e9,
                                      "ms": statistics.median(ms)}
         del xs, cs, ss, outs
@@ -595,10 +627,12 @@ def run_extras(dev, peaks):
     def fr_q(i):
         j = i % 4
         ops.rope_quantize_into(xs[j], cs[j], ss[j], cb, G, 4, fr, pos)
-    ms = _time_events(fr_q, 20)
+    ms = _time_graph(fr_q, 20)
     byts = LK * H_TOTAL * quant_bytes_per_row(G)
     res["rope_quantize_append_block_4680_per_tensor"] = {
-        "gbs": byts / (statistics.median(ms) / 1e3) / 1e9, "ms": statistics.median(ms), "bytes": byts}
+        "gbs": byts / (statistics.median(ms) / 1e3) / 1e9, "ms": statistics.median(ms), "bytes": byts,
+        "frac_hbm": byts / (statistics.median(ms) / 1e3) / 1e9 / peaks["hbm_gbs"],
+        "timing": "CUDA graph of 20 launches"}
     del xs, cs, ss
     torch.cuda.empty_cache()
 
@@ -611,12 +645,12 @@ def run_extras(dev, peaks):
     def fl(i):
         j = 2 * (i % 4)
         ops.quantize_layers_into(xs[j:j + 2], cs[j:j + 2], ss[j:j + 2], cb, G, 4)
-    ms = _time_events(fl, 20)
+    ms = _time_graph(fl, 20)
     byts = 2 * LK * H_TOTAL * quant_bytes_per_row(G)
     gbs = byts / (statistics.median(ms) / 1e3) / 1e9
     res["quantize_append_layer_kv_4680_one_launch"] = {
         "gbs": gbs, "ms": statistics.median(ms), "bytes": byts, "frac_hbm": gbs / peaks["hbm_gbs"],
-        "note": "4 rotating input pairs (384 MB > L2)"}
+        "note": "4 rotating input pairs (384 MB > L2); CUDA graph of 20 launches"}
     del xs, cs, ss
     torch.cuda.empty_cache()
 
@@ -877,6 +911,27 @@ def run_profile_case(case: str, launches: int = 6):
         out = torch.empty_like(q)
         for _ in range(launches):
             ops.attention_packed(q, tk, tv, 0, LK, out=out)
+    elif case in ("append", "rope"):
+        # one block of 4680 tokens x 40 heads: K and V by two launches, by one launch,
+        # the rotate + quantize of the keys, and the block's read back (dequantize)
+        from kvq import rope
+        bands = quant_kv._band_edges(D, MODE)
+        G = len(bands)
+        cb = quant_kv_kernels.host_chan_band(quant_kv_kernels.build_chan_band(bands, D, "cpu"))
+        xs = [synth.make_k(LK, H_TOTAL, seed=70 + i, device=dev) for i in range(2)]
+        cs = [torch.empty((LK, H_TOTAL, D // 2), dtype=torch.uint8, device=dev) for _ in range(2)]
+        ss = [torch.empty((LK, H_TOTAL, G), dtype=torch.bfloat16, device=dev) for _ in range(2)]
+        fr = rope.freqs(1024, device=dev)
+        pos = rope.grid_positions(0, LK, device=dev)
+        for _ in range(launches):
+            if case == "rope":
+                ops.rope_quantize_into(xs[0], cs[0], ss[0], cb, G, 4, fr, pos)
+                continue
+            for t in range(2):
+                ops.quantize_into(xs[t], cs[t], ss[t], cb, G, 4)
+            ops.quantize_layers_into(xs, cs, ss, cb, G, 4)
+            ops.rope_quantize_into(xs[0], cs[0], ss[0], cb, G, 4, fr, pos)
+            ops.dequantize_into(cs[1], ss[1], xs[1], cb, G, 4)
     else:
         bands = quant_kv._band_edges(D, MODE)
         G = len(bands)
@@ -906,7 +961,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--gather", default="fused", choices=("fused", "nccl"),
                     help="N > 1: all-gather of the output in the attention epilogue, or by NCCL")
-    ap.add_argument("--profile-case", choices=("attention", "quantize", "dequantize"),
+    ap.add_argument("--profile-case", choices=("attention", "quantize", "dequantize", "append", "rope"),
                     help="run a few launches of one kernel for an ncu capture and exit")
     args = ap.parse_args()
     if args.profile_case:

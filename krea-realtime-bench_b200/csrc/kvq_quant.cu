@@ -295,6 +295,8 @@ __global__ void __launch_bounds__(kQR, 3) quantize_rows_pipe(const __grid_consta
   uint16_t* sm_sc = reinterpret_cast<uint16_t*>(smem_raw + S * kQR * 256 + kQR * CW);  // kQR x G
   const int tid = threadIdx.x;
   const uint32_t in_base = static_cast<uint32_t>(__cvta_generic_to_shared(sm_in));
+  pdl_wait();
+  pdl_launch_dependents();
 
   // A launch tile is (tensor ti, tile loc of it). The grid-stride walk advances
   // (ti, loc) by additions; a division only places the first tiles.
@@ -598,6 +600,8 @@ __global__ void __launch_bounds__(kQT, 3) dequantize_rows_pipe(DequantArgs a, in
   const uint32_t code_base = static_cast<uint32_t>(__cvta_generic_to_shared(smem_raw + kQT * 256));
   const uint4* sm_code = reinterpret_cast<const uint4*>(smem_raw + kQT * 256);  // kDStages x kQT x 4 chunks
   const int tid = threadIdx.x;
+  pdl_wait();
+  pdl_launch_dependents();
 
   auto issue = [&](int64_t tile, int stage) {
     const int64_t row0 = tile * kQT;
@@ -726,7 +730,11 @@ static int launch_fast(const P& b, int64_t tiles, cudaStream_t st) {
   }
   const int64_t cap = static_cast<int64_t>(per_sm) * num_sms();
   const unsigned grid = static_cast<unsigned>(tiles < cap ? tiles : cap);
-  quantize_rows_pipe<L, BITS, P, ROPE><<<grid, kQR, smem, st>>>(b, tiles);
+  cudaError_t e = launch_pdl(quantize_rows_pipe<L, BITS, P, ROPE>, grid, kQR, smem, st, b, tiles);
+  if (e != cudaSuccess) {
+    set_error("kvq_quantize: launch failed: %s", cudaGetErrorString(e));
+    return KVQ_ERR_CUDA;
+  }
   return check_launch("kvq_quantize");
 }
 
@@ -760,7 +768,12 @@ static int launch_dequant(const DequantArgs& a, cudaStream_t st) {
   }
   const int64_t tiles = (a.n_rows + kQT - 1) / kQT;
   const int64_t cap = 3LL * num_sms();
-  dequantize_rows_pipe<L><<<static_cast<unsigned>(tiles < cap ? tiles : cap), kQT, smem, st>>>(a, tiles);
+  cudaError_t e = launch_pdl(dequantize_rows_pipe<L>, static_cast<unsigned>(tiles < cap ? tiles : cap), kQT, smem,
+                             st, a, tiles);
+  if (e != cudaSuccess) {
+    set_error("kvq_dequantize: launch failed: %s", cudaGetErrorString(e));
+    return KVQ_ERR_CUDA;
+  }
   return check_launch("kvq_dequantize");
 }
 

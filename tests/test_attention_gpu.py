@@ -239,9 +239,11 @@ def test_attention_stats_match_fp32_softmax(B, S, H, Lq, lo, hi, sink, mode):
     q = synth.make_q(B, Lq, H, seed=43)
     out, st = quant_kv.attention_stats(q.cuda(), tk[:, lo:hi], tv[:, lo:hi])
     plain = quant_kv.attention(q.cuda(), tk[:, lo:hi], tv[:, lo:hi])
-    assert torch.equal(out.view(torch.int16), plain.view(torch.int16))      # same attention result
+    assert torch.equal(out.view(torch.int16), plain.view(torch.int16))      # same attention arithmetic
     bands = ko.band_edges(128, mode)
     kw = np.stack([_oracle_window(kb[b], bands, sink, lo, hi) for b in range(B)])
+    vw = np.stack([_oracle_window(vb[b], bands, sink, lo, hi) for b in range(B)])
+    _check(out, _oracle_attention(_u16(q), kw, vw), "attention output of the statistics kernel")
     qf = torch.from_numpy(ko.bf16_to_f32(_u16(q))).double()
     kf = torch.from_numpy(ko.bf16_to_f32(kw)).double()
     logits = torch.einsum("bqhd,bkhd->bqhk", qf, kf) / math.sqrt(128)

@@ -17,12 +17,15 @@ def _u16(t):
 
 
 @pytest.mark.parametrize("mode,bits", [("bands4", 4), ("bands", 4), ("blind64", 8)])
-@pytest.mark.parametrize("B,S,a,b,sink,t0", [(1, 4680, 0, 4680, 1560, 0), (2, 3000, 1200, 2901, 1500, 9360),
-                                             (1, 500, 7, 8, 0, 77)])
-def test_rope_quantize_matches_oracle(mode, bits, B, S, a, b, sink, t0):
+@pytest.mark.parametrize("B,S,a,b,sink,t0,H", [(1, 4680, 0, 4680, 1560, 0, 5), (2, 3000, 1200, 2901, 1500, 9360, 5),
+                                               (1, 500, 7, 8, 0, 77, 5),
+                                               # 16 heads or more: a 128-row tile spans at most 9 tokens; up to
+                                               # 8 tokens the (cos, sin) of the tile are gathered once
+                                               (1, 4680, 0, 4680, 1560, 0, 40), (2, 1000, 33, 901, 100, 3120, 40),
+                                               (1, 700, 5, 690, 64, 1560, 16), (1, 300, 0, 300, 0, 0, 18)])
+def test_rope_quantize_matches_oracle(mode, bits, B, S, a, b, sink, t0, H):
     import quant_kv
     from kvq import rope
-    H = 5
     c = quant_kv.QuantKVTensor([B, S, H, 128], "cuda", torch.bfloat16, bits, mode, sink)
     g = torch.Generator().manual_seed(b + t0)
     x = (torch.randn(B, b - a, H, 128, generator=g) * torch.exp(torch.randn(H, 128, generator=g))).to(torch.bfloat16)
@@ -51,3 +54,31 @@ def test_rope_quantize_rejects_bad_arguments():
         ops.rope_quantize_into(x, codes, scales, cb, 12, 4, fr, torch.zeros(8, 2, dtype=torch.int32, device="cuda"))
     with pytest.raises(ValueError):   # float32 table
         ops.rope_quantize_into(x, codes, scales, cb, 12, 4, fr.float(), rope.grid_positions(0, 8, device="cuda"))
+
+
+def test_rope_quantize_special_values():
+    """Zeros (both signs), subnormals and values near 2^126 (finite after the rotation) in the
+    keys before rotation take the exact widening path of the kernel; codes, scales
+    and sink rows stay bit-identical to the oracle (40 heads: the tile's (cos, sin)
+    come from shared memory)."""
+    import quant_kv
+    from kvq import rope
+    S, H = 600, 40
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(S, H, 128, generator=g).to(torch.bfloat16)
+    bits = x.view(torch.int16)
+    specials = torch.tensor([0x0000, 0x8000, 0x0001, 0x807F, 0x0040, 0x7E7F, 0xFE7F, 0x0080, 0x8080],
+                            dtype=torch.int32).to(torch.int16)
+    idx = torch.randint(0, S * H * 128, (4000,), generator=g)
+    bits.view(-1)[idx] = specials[torch.arange(4000) % len(specials)]
+    x[17] = 0                                   # a whole row of zeros (scale 1 path)
+    c = quant_kv.QuantKVTensor([1, S, H, 128], "cuda", torch.bfloat16, 4, "bands4", 200)
+    fr = rope.freqs(1024)
+    pos = rope.grid_positions(3000, S)
+    c.write_rope_(0, S, x.unsqueeze(0).cuda(), fr.cuda(), pos.cuda())
+    bands = ko.band_edges(128, "bands4")
+    xr = ko.rope_f64(_u16(x), fr.numpy(), pos.numpy())
+    codes, scales = c_oracle.quantize(xr, bands)
+    assert np.array_equal(c.packed.cpu().numpy(), codes)
+    assert np.array_equal(_u16(c.scales), scales)
+    assert np.array_equal(_u16(c.sink), xr[:200])
