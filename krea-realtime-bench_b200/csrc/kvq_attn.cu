@@ -300,6 +300,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   const long long lim = a.wait_cycles;
+  pdl_wait();
+  pdl_launch_dependents();
   // One CTA per (pair of Q tiles, head, stream), 1-D grid. The CTAs with two Q
   // tiles come first, pairs fastest (a head's packed K/V stays in L2 across its
   // pairs); the last pairs that hold at most BM queries (one Q tile, about half
@@ -833,7 +835,12 @@ int launch(const Args& a, int n_ctas, int batch, cudaStream_t st) {
     }
     configured[dev] = true;
   }
-  attention_kernel<L, KB, STATS><<<n_ctas * a.H * batch, kThreads, kSmemBytes, st>>>(a);
+  cudaError_t e = launch_pdl(attention_kernel<L, KB, STATS>, static_cast<unsigned>(n_ctas * a.H * batch), kThreads,
+                             kSmemBytes, st, a);
+  if (e != cudaSuccess) {
+    set_error("kvq_attention: launch failed: %s", cudaGetErrorString(e));
+    return KVQ_ERR_CUDA;
+  }
   return check_launch("kvq_attention");
 }
 
