@@ -905,12 +905,21 @@ def run_profile_case(case: str, launches: int = 6):
     from kvq import ops, synth
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    if case == "attention":
+    if case in ("attention", "attention_gather", "attention_stats"):
+        # window 3 (config 1); the gather instance stores into two local [1, 4680, 80, 128]
+        # buffers at head offset 20, the statistics instance also writes the row statistics
         tk, tv, _, _ = make_caches(1, LK, H_TOTAL, SINK, dev, seed=1)
         q = synth.make_q(1, LQ, H_TOTAL, seed=2, device=dev)
         out = torch.empty_like(q)
+        bufs = [torch.empty((1, LQ, 2 * H_TOTAL, D), dtype=torch.bfloat16, device=dev) for _ in range(2)]
+        st = torch.empty((1, LQ, H_TOTAL, 4), dtype=torch.float32, device=dev)
         for _ in range(launches):
-            ops.attention_packed(q, tk, tv, 0, LK, out=out)
+            if case == "attention":
+                ops.attention_packed(q, tk, tv, 0, LK, out=out)
+            elif case == "attention_gather":
+                ops.attention_packed_gather(q, tk, tv, 0, LK, [b.data_ptr() for b in bufs], 20, 2 * H_TOTAL)
+            else:
+                ops.attention_packed(q, tk, tv, 0, LK, out=out, stats=st)
     elif case in ("append", "rope"):
         # one block of 4680 tokens x 40 heads: K and V by two launches, by one launch,
         # the rotate + quantize of the keys, and the block's read back (dequantize)
@@ -961,7 +970,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--gather", default="fused", choices=("fused", "nccl"),
                     help="N > 1: all-gather of the output in the attention epilogue, or by NCCL")
-    ap.add_argument("--profile-case", choices=("attention", "quantize", "dequantize", "append", "rope"),
+    ap.add_argument("--profile-case", choices=("attention", "attention_gather", "attention_stats", "quantize",
+                                               "dequantize", "append", "rope"),
                     help="run a few launches of one kernel for an ncu capture and exit")
     args = ap.parse_args()
     if args.profile_case:
