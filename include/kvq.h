@@ -108,6 +108,14 @@ KVQ_API int kvq_dequantize(const void* codes, const void* scales, const void* si
  *   lo, hi     window of cache tokens; tokens < sink_tokens come from the sinks
  *   out        bf16 [batch][n_q][n_heads][head_dim], token stride out_token_stride
  *   softmax_scale  <= 0 selects 1/sqrt(head_dim)
+ *   workspace  NULL, or device memory of workspace_bytes bytes (256-byte aligned)
+ *              that kvq_attention_workspace_bytes() asks for: with it, the units
+ *              of the launch's last wave are cut along the KV window into parts
+ *              whose partial results the last part to finish merges (the
+ *              workspace holds them, and a counter per unit that the launch
+ *              clears first); launches that share a workspace must be ordered
+ *              (one stream). Without it, or when it is too small, every unit
+ *              runs whole; the results agree within the attention tolerance.
  * head_dim 128; K int4 (k_bits 4) or int8 (k_bits 8, the K8V4 mode of
  * bench_qkv.py:160) and V int4; the five reference group layouts.
  */
@@ -117,7 +125,16 @@ KVQ_API int kvq_attention(const void* q, int64_t q_token_stride,
                           int64_t cache_tokens, int64_t sink_tokens, int64_t lo, int64_t hi,
                           void* out, int64_t out_token_stride, int batch, int64_t n_q,
                           int n_heads, int head_dim, const int32_t* chan_band, int n_groups,
-                          int k_bits, int v_bits, float softmax_scale, void* stream);
+                          int k_bits, int v_bits, float softmax_scale, void* workspace,
+                          int64_t workspace_bytes, void* stream);
+
+/*
+ * Bytes of workspace kvq_attention() / kvq_attention_gather() use for a launch
+ * of this shape on the current device (0: the launch runs every unit whole), in
+ * *bytes. No counterpart in the reference (its attention is a library call).
+ */
+KVQ_API int kvq_attention_workspace_bytes(int batch, int64_t n_q, int n_heads, int64_t n_kv_tokens,
+                                          int64_t* bytes);
 
 /*
  * kvq_attention() that also writes, per (stream, query, head), four fp32 row
@@ -192,7 +209,8 @@ KVQ_API int kvq_attention_gather(const void* q, int64_t q_token_stride,
                                  void* const* outs, int n_outs, int out_head0, int out_heads,
                                  int64_t out_token_stride, int batch, int64_t n_q,
                                  int n_heads, int head_dim, const int32_t* chan_band, int n_groups,
-                                 int k_bits, int v_bits, float softmax_scale, void* stream);
+                                 int k_bits, int v_bits, float softmax_scale, void* workspace,
+                                 int64_t workspace_bytes, void* stream);
 
 /*
  * Device-side barrier of the ranks of a head-sharded job, stream-ordered: one

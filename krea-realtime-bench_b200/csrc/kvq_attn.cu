@@ -58,7 +58,11 @@
 #include <cuda.h>
 #include <cuda_bf16.h>
 
+#include <algorithm>
 #include <cstring>
+#include <mutex>
+#include <queue>
+#include <vector>
 #include <type_traits>
 #include <utility>
 
@@ -135,6 +139,16 @@ struct alignas(64) Args {
   float scale_log2;
   long long wait_cycles;  // limit of every bounded wait (kWaitCycles unless a test asks for less)
   int stall_tile;         // >= 0 only in the abort test: the K producer stops before this KV tile
+  // Work units (see attention_kernel): n_hb = heads x streams; the last split_full
+  // two-tile units run as two halves of their KV window, every one-tile unit as
+  // split_single parts (1 = whole); parts exchange partial results through ws and
+  // count in ctr[unit]. ws holds slots of float4 [33][128 rows] (a Q tile's O
+  // rows in 32 chunks of 4 channels, then (m, l)): split two-tile unit u, part p,
+  // Q tile x at slot (2u + p) 2 + x; one-tile unit s (unit split_full + s), part p
+  // at slot 4 split_full + s split_single + p.
+  int n_hb, split_full, split_single;
+  float4* ws;
+  unsigned* ctr;
 };
 
 // byte offset of 16-byte chunk c (8 bf16 columns) of row r in a 64 x 128 bf16
@@ -281,6 +295,13 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return d;
 }
 
+// Workspace slot (float4 [33][128] each) of Q tile x of part p of split unit u.
+__host__ __device__ __forceinline__ int64_t ws_slot(const Args& a, int u, int p, int x) {
+  return u < a.split_full ? (static_cast<int64_t>(u) * 2 + p) * 2 + x
+                          : static_cast<int64_t>(4) * a.split_full +
+                                static_cast<int64_t>(u - a.split_full) * a.split_single + p;
+}
+
 template <class L, int KB, bool STATS>
 __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_constant__ Args a) {
   using GEO = Geo<KB>;
@@ -307,22 +328,48 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
   // pairs); the last pairs that hold at most BM queries (one Q tile, about half
   // the work) come after all of them, so that they fill the last wave instead of
   // leaving a partial wave of full-length CTAs at the end.
+  //
+  // Wave balance: the last split_full two-tile units are each run by two CTAs,
+  // one per half of the KV window (consecutive block indices), and every one-tile
+  // unit by split_single CTAs (one per part of the KV window): finer pieces for
+  // the last wave. A part is an ordinary CTA on a sub-window of whole KV tiles; it
+  // leaves its unnormalised O, row max and row sum in the workspace, and the part
+  // that finishes last merges them (after the CTA's final barrier, below).
   const int n_pairs = (a.Lq + 2 * BM - 1) / (2 * BM);
   const int n_full = a.Lq - (n_pairs - 1) * 2 * BM > BM ? n_pairs : n_pairs - 1;
-  const int n_hb = static_cast<int>(gridDim.x) / n_pairs;  // heads x streams
-  int pair, hb;
-  if (static_cast<int>(blockIdx.x) < n_full * n_hb) {
-    hb = static_cast<int>(blockIdx.x) / n_full;
-    pair = static_cast<int>(blockIdx.x) - hb * n_full;
+  const int n_hb = a.n_hb;  // heads x streams
+  const int n_ft = n_full * n_hb;
+  const int n_a = n_ft - a.split_full;  // two-tile units run whole
+  const int bid = static_cast<int>(blockIdx.x);
+  int pair, hb, part = 0, parts = 1, unit = -1;
+  if (bid < n_a) {
+    hb = bid / n_full;
+    pair = bid - hb * n_full;
+  } else if (bid < n_ft + a.split_full) {
+    const int v = bid - n_a, u = n_a + (v >> 1);
+    hb = u / n_full;
+    pair = u - hb * n_full;
+    part = v & 1;
+    parts = 2;
+    unit = v >> 1;
   } else {
-    hb = static_cast<int>(blockIdx.x) - n_full * n_hb;
+    const int w = bid - (n_ft + a.split_full);
+    hb = w / a.split_single;
+    part = w - hb * a.split_single;
+    parts = a.split_single;
     pair = n_pairs - 1;
+    if (parts > 1) unit = a.split_full + hb;
   }
   const int q0 = pair * (2 * BM);
   const int h = hb % a.H;
   const int b = hb / a.H;
   const int nq = a.Lq - q0 > BM ? 2 : 1;  // Q tiles with queries
-  const int nkv = (a.Lk + BN - 1) / BN;
+  // this CTA's KV window: tiles [jb, je) of the launch's window of a.Lk tokens from a.lo
+  const int nkv_all = (a.Lk + BN - 1) / BN;
+  const int jb = part * nkv_all / parts, je = (part + 1) * nkv_all / parts;
+  const int64_t lo = a.lo + static_cast<int64_t>(jb) * BN;
+  const int Lk = min(je * BN, a.Lk) - jb * BN;
+  const int nkv = je - jb;
 
   if (tid == 0) {
     for (int i = 0; i < 2 * NS_LD; ++i) {
@@ -471,7 +518,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
       if (STATS) {
         lb += sumb;
         // columns whose cache token is below sink_tokens
-        const int64_t t0 = a.lo + static_cast<int64_t>(j) * BN;
+        const int64_t t0 = lo + static_cast<int64_t>(j) * BN;
         const int ns = static_cast<int>(max(static_cast<int64_t>(0), min(static_cast<int64_t>(valid), a.sink_tokens - t0)));
         if (ns == valid) {
           ls += sum;
@@ -493,13 +540,28 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
       return true;
     };
     for (int j = 0; j < nkv; ++j) {
-      const int valid = min(BN, a.Lk - j * BN);
+      const int valid = min(BN, Lk - j * BN);
       if (!(valid == BN ? step(j, valid, std::false_type{}) : step(j, valid, std::true_type{}))) {
         ok = false;
         break;
       }
     }
-    if (ok && mbar_wait_warp(&bars[bOFinal + x], 0, abort, &g_attn_status, lim)) {
+    if (ok && parts > 1 && mbar_wait_warp(&bars[bOFinal + x], 0, abort, &g_attn_status, lim)) {
+      // one part of a split unit: leave the unnormalised O row, m and l for the merge
+      tc_fence_after();
+      float4* dst = a.ws + ws_slot(a, unit, part, x) * 33 * BM + r;
+#pragma unroll 1
+      for (int k = 0; k < 4; ++k) {
+        uint32_t o[32];
+        tmem_ld32_wait(tO + 32 * k, o);
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          dst[(8 * k + c) * BM] = make_float4(__uint_as_float(o[4 * c]), __uint_as_float(o[4 * c + 1]),
+                                              __uint_as_float(o[4 * c + 2]), __uint_as_float(o[4 * c + 3]));
+      }
+      dst[32 * BM] = make_float4(m, l, 0.0f, 0.0f);
+      __threadfence();
+    } else if (ok && mbar_wait_warp(&bars[bOFinal + x], 0, abort, &g_attn_status, lim)) {
       tc_fence_after();
       const float inv = 1.0f / l;
       if (STATS && qi < a.Lq) {
@@ -586,8 +648,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
     // this row's scales of tile j + 1 are loaded while tile j is converted
     auto load_sw = [&](int jj, ScaleWords<L>& sw) {
       const int jt = jj * BN + r;
-      const int64_t tok = a.lo + jt;
-      if (jj < nkv && jt < a.Lk && tok >= a.sink_tokens)
+      const int64_t tok = lo + jt;
+      if (jj < nkv && jt < Lk && tok >= a.sink_tokens)
         load_scale_words<L>(scales + ((static_cast<int64_t>(b) * a.cache_tokens + tok) * a.H + h) * L::G, sw);
     };
     ScaleWords<L> sw_next;
@@ -595,8 +657,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
     for (int j = 0; j < nkv; ++j) {
       const int ls = j % NS_LD, ks = j % NS_KV;
       const int jt = j * BN + r;
-      const int64_t tok = a.lo + jt;
-      const bool live = jt < a.Lk;
+      const int64_t tok = lo + jt;
+      const bool live = jt < Lk;
       const bool coded = live && tok >= a.sink_tokens;
       const ScaleWords<L> sw = sw_next;
       load_sw(j + 1, sw_next);
@@ -666,8 +728,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
         if (j >= NS_LD &&
             !mbar_wait(&bars[bLdEmpty + pv * NS_LD + ls], ((j / NS_LD) - 1) & 1, abort, &g_attn_status, lim))
           break;
-        const int64_t t0 = a.lo + static_cast<int64_t>(j) * BN;
-        const int64_t t1 = a.lo + min(static_cast<int64_t>(j + 1) * BN, static_cast<int64_t>(a.Lk));
+        const int64_t t0 = lo + static_cast<int64_t>(j) * BN;
+        const int64_t t1 = lo + min(static_cast<int64_t>(j + 1) * BN, static_cast<int64_t>(Lk));
         const bool has_sink = t0 < a.sink_tokens;
         const bool has_codes = t1 > a.sink_tokens;
         if (has_sink && j >= NS_KV &&
@@ -767,6 +829,86 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
+  if (parts > 1) {
+    // The part that finishes last merges the unit: every part's partial row is in
+    // the workspace (written and fenced before the barrier above), so after the
+    // atomic count this CTA reads them all, combines them in base-2 exponent
+    // space, normalises and stores the output tile as the whole units do.
+    volatile int* last = reinterpret_cast<volatile int*>(smem + kOffMisc + 16);
+    if (tid == 0) {
+      int is_last = 0;
+      if (!*abort) {
+        const unsigned old = atomicAdd(&a.ctr[unit], 1u);
+        is_last = old == static_cast<unsigned>(parts - 1);
+        if (is_last) a.ctr[unit] = 0u;  // ready for the next launch
+      }
+      *last = is_last;
+    }
+    __syncthreads();
+    if (*last) {
+      __threadfence();
+      if (warp < 4 * nq) {
+        const int x = warp >> 2;
+        const int r = tid - x * BM;
+        const float4* src = a.ws + ws_slot(a, unit, 0, x) * 33 * BM + r;
+        // float4s from one part's slot to the next
+        const int64_t pstride = (unit < a.split_full ? 2 : 1) * static_cast<int64_t>(33) * BM;
+        float wp[4];
+        float mx = -INFINITY, L = 0.0f;
+#pragma unroll
+        for (int p = 0; p < 4; ++p)
+          if (p < parts) mx = fmaxf(mx, __ldcg(src + p * pstride + 32 * BM).x);
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          wp[p] = 0.0f;
+          if (p < parts) {
+            const float4 ml = __ldcg(src + p * pstride + 32 * BM);
+            wp[p] = ex2(ml.x - mx);
+            L = fmaf(ml.y, wp[p], L);
+          }
+        }
+        const float inv = 1.0f / L;
+        const uint32_t stage = sbase + kOffQ + x * kQTile;
+#pragma unroll 1
+        for (int ch = 0; ch < 16; ++ch) {  // 8 output channels per 16-byte chunk
+          float acc[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[e] = 0.0f;
+#pragma unroll
+          for (int p = 0; p < 4; ++p) {
+            if (p < parts) {
+              const float4 v0 = __ldcg(src + p * pstride + (2 * ch) * BM);
+              const float4 v1 = __ldcg(src + p * pstride + (2 * ch + 1) * BM);
+              acc[0] = fmaf(v0.x, wp[p], acc[0]);
+              acc[1] = fmaf(v0.y, wp[p], acc[1]);
+              acc[2] = fmaf(v0.z, wp[p], acc[2]);
+              acc[3] = fmaf(v0.w, wp[p], acc[3]);
+              acc[4] = fmaf(v1.x, wp[p], acc[4]);
+              acc[5] = fmaf(v1.y, wp[p], acc[5]);
+              acc[6] = fmaf(v1.z, wp[p], acc[6]);
+              acc[7] = fmaf(v1.w, wp[p], acc[7]);
+            }
+          }
+          st_shared_v4(stage + (ch >> 3) * kQAtom + r * 128 + (((ch & 7) ^ (r & 7)) << 4),
+                       make_uint4(pack_bf16x2(acc[0] * inv, acc[1] * inv), pack_bf16x2(acc[2] * inv, acc[3] * inv),
+                                  pack_bf16x2(acc[4] * inv, acc[5] * inv), pack_bf16x2(acc[6] * inv, acc[7] * inv)));
+        }
+        fence_proxy_async_smem();
+      }
+      __syncthreads();
+      if (tid < nq * BM && (tid & (BM - 1)) == 0) {
+        const int x = tid / BM;
+        const uint32_t stage = sbase + kOffQ + x * kQTile;
+        const int xq = (a.out_head0 + h) * D, yq = q0 + x * BM;
+        for (int d = 0; d < a.n_out; ++d) {
+          tma_store_3d(&a.tm_out[d], stage, xq, yq, b);
+          tma_store_3d(&a.tm_out[d], stage + kQAtom, xq + 64, yq, b);
+        }
+        bulk_commit();
+        bulk_wait_read_all();
+      }
+    }
+  }
 }
 
 // ---------------------------------------------------------------- host side
@@ -820,6 +962,99 @@ static int make_out_map(CUtensorMap* m, void* base, uint64_t row_elems, uint64_t
   return KVQ_OK;
 }
 
+// ---------------------------------------------------------------- wave balance
+// How the units of a launch are cut for the last wave (Args: split_full,
+// split_single), and the workspace the parts need.
+struct SplitPlan {
+  int split_full = 0, split_single = 1, units = 0;
+  int64_t ws_bytes = 0, ctr_offset = 0;
+};
+
+// Makespan, in units of a two-tile CTA's time, of list-scheduling `n_whole`
+// two-tile CTAs, then `2 k2` halves, then `P n_single` parts of the one-tile
+// CTAs on `sms` SMs, in that order (the order of the block indices). Costs:
+// two-tile 1, one-tile 0.82 (its per-tile pace is set by the KV pipeline, not
+// by its one Q tile), a part its share plus 0.04 for the partial store and merge.
+static double makespan(int n_whole, int k2, int n_single, int P, int sms) {
+  std::vector<double> t(static_cast<size_t>(sms), 0.0);
+  std::priority_queue<double, std::vector<double>, std::greater<double>> h(t.begin(), t.end());
+  auto run = [&](int n, double c) {
+    for (int i = 0; i < n; ++i) {
+      const double f = h.top();
+      h.pop();
+      h.push(f + c);
+    }
+  };
+  run(n_whole, 1.0);
+  run(2 * k2, 0.5 + 0.04);
+  run(P * n_single, P == 1 ? 0.82 : 0.82 / P + 0.04);
+  double m = 0.0;
+  while (!h.empty()) {
+    m = std::max(m, h.top());
+    h.pop();
+  }
+  return m;
+}
+
+static SplitPlan plan_split(int64_t n_q, int n_hb, int64_t n_kv, int sms) {
+  SplitPlan p;
+  const int n_pairs = static_cast<int>((n_q + 2 * BM - 1) / (2 * BM));
+  const int n_full = n_q - static_cast<int64_t>(n_pairs - 1) * 2 * BM > BM ? n_pairs : n_pairs - 1;
+  const int n_ft = n_full * n_hb, n_s = (n_pairs - n_full) * n_hb;
+  const int nkv = static_cast<int>((n_kv + BN - 1) / BN);
+  if (nkv < 2 || n_ft + n_s > 64 * sms) return p;  // nothing to split, or the tail is a small share
+  struct Key {
+    int n_ft, n_s, nkv, sms;
+  };
+  static std::mutex mu;
+  static std::vector<std::pair<Key, SplitPlan>> cache;
+  {
+    std::lock_guard<std::mutex> g(mu);
+    for (auto& e : cache)
+      if (e.first.n_ft == n_ft && e.first.n_s == n_s && e.first.nkv == nkv && e.first.sms == sms) return e.second;
+  }
+  const double base = makespan(n_ft, 0, n_s, 1, sms);
+  double best = base;
+  int best_k = 0, best_p = 1;
+  for (int P = 1; P <= 4 && P <= nkv; P *= 2) {
+    if (P > 1 && n_s == 0) break;
+    for (int k = 0; k <= std::min(n_ft, 2 * sms); k += 4) {
+      const double m = makespan(n_ft - k, k, n_s, P, sms);
+      if (m < best - 1e-9) {
+        best = m;
+        best_k = k;
+        best_p = P;
+      }
+    }
+  }
+  if (best < base * 0.99) {  // worth the partial stores
+    p.split_full = best_k;
+    p.split_single = best_p;
+    p.units = best_k + (best_p > 1 ? n_s : 0);
+    const int64_t slots = static_cast<int64_t>(4) * best_k + (best_p > 1 ? static_cast<int64_t>(n_s) * best_p : 0);
+    const int64_t f4 = slots * 33 * BM;
+    p.ctr_offset = (f4 * 16 + 255) / 256 * 256;
+    p.ws_bytes = p.ctr_offset + static_cast<int64_t>(p.units) * 4;
+  }
+  std::lock_guard<std::mutex> g(mu);
+  if (cache.size() >= 64) cache.erase(cache.begin());
+  cache.push_back({Key{n_ft, n_s, nkv, sms}, p});
+  return p;
+}
+
+static int num_sms() {
+  static int sms[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (sms[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    sms[dev] = n;
+  }
+  return sms[dev];
+}
+
 template <class L, int KB, bool STATS>
 int launch(const Args& a, int n_ctas, int batch, cudaStream_t st) {
   constexpr int kSmemBytes = Geo<KB>::kSmemBytes;
@@ -835,7 +1070,8 @@ int launch(const Args& a, int n_ctas, int batch, cudaStream_t st) {
     }
     configured[dev] = true;
   }
-  cudaError_t e = launch_pdl(attention_kernel<L, KB, STATS>, static_cast<unsigned>(n_ctas * a.H * batch), kThreads,
+  (void)batch;
+  cudaError_t e = launch_pdl(attention_kernel<L, KB, STATS>, static_cast<unsigned>(n_ctas), kThreads,
                              kSmemBytes, st, a);
   if (e != cudaSuccess) {
     set_error("kvq_attention: launch failed: %s", cudaGetErrorString(e));
@@ -862,7 +1098,8 @@ static int attention_impl(const void* q, int64_t q_token_stride, const void* k_c
                           int n_outs, int out_head0, int out_heads, int64_t out_token_stride, int batch, int64_t n_q,
                           int n_heads, int head_dim, const int32_t* chan_band, int n_groups, int k_bits, int v_bits,
                           float softmax_scale, void* stream, bool tma_out, float* stats,
-                          long long wait_cycles = sm100::kWaitCycles, int stall_tile = -1) {
+                          long long wait_cycles = sm100::kWaitCycles, int stall_tile = -1,
+                          void* workspace = nullptr, int64_t workspace_bytes = 0) {
   KVQ_REQUIRE(head_dim == 128, KVQ_ERR_UNSUPPORTED, "attention supports head_dim 128, got %d", head_dim);
   KVQ_REQUIRE((k_bits == 4 || k_bits == 8) && v_bits == 4, KVQ_ERR_UNSUPPORTED,
               "attention reads int4 or int8 K and int4 V (got %d/%d bits)",
@@ -961,8 +1198,30 @@ static int attention_impl(const void* q, int64_t q_token_stride, const void* k_c
   a.scale_log2 = sc * 1.4426950408889634f;
   a.wait_cycles = wait_cycles;
   a.stall_tile = stall_tile;
-  const int ctas = static_cast<int>((n_q + 2 * attn::BM - 1) / (2 * attn::BM));
+  a.n_hb = n_heads * batch;
+  a.split_full = 0;
+  a.split_single = 1;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t n_pairs = (n_q + 2 * attn::BM - 1) / (2 * attn::BM);
+  int ctas = static_cast<int>(n_pairs * a.n_hb);
+  if (workspace && stats == nullptr && stall_tile < 0) {
+    const attn::SplitPlan sp = attn::plan_split(n_q, a.n_hb, hi - lo, attn::num_sms());
+    if (sp.units > 0 && workspace_bytes >= sp.ws_bytes) {
+      KVQ_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255) == 0, KVQ_ERR_ALIGN,
+                  "the workspace must be 256-byte aligned");
+      a.split_full = sp.split_full;
+      a.split_single = sp.split_single;
+      a.ws = static_cast<float4*>(workspace);
+      a.ctr = reinterpret_cast<unsigned*>(static_cast<char*>(workspace) + sp.ctr_offset);
+      const int64_t n_full = n_q - (n_pairs - 1) * 2 * attn::BM > attn::BM ? n_pairs : n_pairs - 1;
+      ctas = static_cast<int>(n_full * a.n_hb + sp.split_full + (n_pairs - n_full) * a.n_hb * sp.split_single);
+      cudaError_t e = cudaMemsetAsync(a.ctr, 0, static_cast<size_t>(sp.units) * 4, st);
+      if (e != cudaSuccess) {
+        set_error("kvq_attention: clearing the workspace counters failed: %s", cudaGetErrorString(e));
+        return KVQ_ERR_CUDA;
+      }
+    }
+  }
   switch (layout) {
     case kLayoutBands: return attn::launch_layout<LayoutBands>(a, ctas, batch, st, k_bits, stats != nullptr);
     case kLayoutBands2: return attn::launch_layout<LayoutBands2>(a, ctas, batch, st, k_bits, stats != nullptr);
@@ -982,7 +1241,7 @@ extern "C" int kvq_attention(const void* q, int64_t q_token_stride, const void* 
                              int64_t cache_tokens, int64_t sink_tokens, int64_t lo, int64_t hi, void* out,
                              int64_t out_token_stride, int batch, int64_t n_q, int n_heads, int head_dim,
                              const int32_t* chan_band, int n_groups, int k_bits, int v_bits, float softmax_scale,
-                             void* stream) {
+                             void* workspace, int64_t workspace_bytes, void* stream) {
   clear_error();
   void* outs[1] = {out};
   if (n_q > 0 && !out) {
@@ -991,7 +1250,20 @@ extern "C" int kvq_attention(const void* q, int64_t q_token_stride, const void* 
   }
   return attention_impl(q, q_token_stride, k_codes, k_scales, k_sink, v_codes, v_scales, v_sink, cache_tokens,
                         sink_tokens, lo, hi, outs, 1, 0, n_heads, out_token_stride, batch, n_q, n_heads, head_dim,
-                        chan_band, n_groups, k_bits, v_bits, softmax_scale, stream, true, nullptr);
+                        chan_band, n_groups, k_bits, v_bits, softmax_scale, stream, true, nullptr, sm100::kWaitCycles,
+                        -1, workspace, workspace_bytes);
+}
+
+extern "C" int kvq_attention_workspace_bytes(int batch, int64_t n_q, int n_heads, int64_t n_kv_tokens,
+                                             int64_t* bytes) {
+  clear_error();
+  KVQ_REQUIRE(bytes && batch >= 1 && n_heads >= 1 && n_q >= 0 && n_kv_tokens >= 0, KVQ_ERR_ARG, "bad shape");
+  *bytes = 0;
+  if (n_q == 0 || n_kv_tokens == 0) return KVQ_OK;
+  int rc = require_sm100();
+  if (rc) return rc;
+  *bytes = attn::plan_split(n_q, n_heads * batch, n_kv_tokens, attn::num_sms()).ws_bytes;
+  return KVQ_OK;
 }
 
 extern "C" int kvq_attention_stats(const void* q, int64_t q_token_stride, const void* k_codes,
@@ -1018,11 +1290,13 @@ extern "C" int kvq_attention_gather(const void* q, int64_t q_token_stride, const
                                     int64_t sink_tokens, int64_t lo, int64_t hi, void* const* outs, int n_outs,
                                     int out_head0, int out_heads, int64_t out_token_stride, int batch, int64_t n_q,
                                     int n_heads, int head_dim, const int32_t* chan_band, int n_groups, int k_bits,
-                                    int v_bits, float softmax_scale, void* stream) {
+                                    int v_bits, float softmax_scale, void* workspace, int64_t workspace_bytes,
+                                    void* stream) {
   clear_error();
   return attention_impl(q, q_token_stride, k_codes, k_scales, k_sink, v_codes, v_scales, v_sink, cache_tokens,
                         sink_tokens, lo, hi, outs, n_outs, out_head0, out_heads, out_token_stride, batch, n_q,
-                        n_heads, head_dim, chan_band, n_groups, k_bits, v_bits, softmax_scale, stream, true, nullptr);
+                        n_heads, head_dim, chan_band, n_groups, k_bits, v_bits, softmax_scale, stream, true, nullptr,
+                        sm100::kWaitCycles, -1, workspace, workspace_bytes);
 }
 
 namespace kvq {

@@ -27,13 +27,14 @@ SIGNATURES = {
     "kvq_quantize": (_i32, [_p, _i64, _p, _p, _p, _i64, _i64, _i32, _i32, _p, _i32, _i32, _p]),
     "kvq_dequantize": (_i32, [_p, _p, _p, _i64, _p, _i64, _i64, _i32, _i32, _p, _i32, _i32, _p]),
     "kvq_attention": (_i32, [_p, _i64, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _i64, _i32, _i64,
-                             _i32, _i32, _p, _i32, _i32, _i32, _f32, _p]),
+                             _i32, _i32, _p, _i32, _i32, _i32, _f32, _p, _i64, _p]),
+    "kvq_attention_workspace_bytes": (_i32, [_i32, _i64, _i32, _i64, ctypes.POINTER(_i64)]),
     "kvq_attention_stats": (_i32, [_p, _i64, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _i64, _p, _i32,
                                    _i64, _i32, _i32, _p, _i32, _i32, _i32, _f32, _p]),
     "kvq_rope_quantize": (_i32, [_p, _i64, _p, _p, _p, _i64, _i64, _i32, _i32, _p, _i32, _i32, _p, _i32, _p, _p]),
     "kvq_rebuild_layers": (_i32, [_i32, _p, _i64, _p, _p, _p, _i64, _i64, _i32, _i32, _p, _i32, _i32, _p]),
     "kvq_attention_gather": (_i32, [_p, _i64, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _i32, _i32, _i32,
-                                    _i64, _i32, _i64, _i32, _i32, _p, _i32, _i32, _i32, _f32, _p]),
+                                    _i64, _i32, _i64, _i32, _i32, _p, _i32, _i32, _i32, _f32, _p, _i64, _p]),
     "kvq_gather_barrier": (_i32, [_p, _i32, _i32, ctypes.c_uint, _i64, _p]),
     "kvq_ipc_export": (_i32, [_p, _p, ctypes.POINTER(_i64)]),
     "kvq_ipc_import": (_i32, [_p, _i64, ctypes.POINTER(_p), ctypes.POINTER(_p)]),

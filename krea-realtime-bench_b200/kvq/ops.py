@@ -198,6 +198,29 @@ def dequantize_into(codes: torch.Tensor, scales: torch.Tensor, out: torch.Tensor
     return out
 
 
+# Per (device, stream) workspace of the attention launches (kvq_attention's
+# wave-balance parts): grown when a launch needs more, reused in stream order.
+_WORKSPACES: dict = {}
+
+
+def _workspace(dev: torch.device, B: int, Lq: int, H: int, n_kv: int):
+    """(pointer, bytes) of a workspace for an attention launch of this shape on the
+    current stream of `dev`, or (None, 0) when the launch runs every unit whole."""
+    need = ctypes.c_int64()
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().kvq_attention_workspace_bytes(B, Lq, H, n_kv, ctypes.byref(need)),
+                   "kvq_attention_workspace_bytes")
+    if need.value == 0:
+        return None, 0
+    key = (dev.index, torch.cuda.current_stream(dev).cuda_stream)
+    buf = _WORKSPACES.get(key)
+    if buf is None or buf.numel() < need.value:
+        buf = torch.empty(need.value + 256, dtype=torch.uint8, device=dev)
+        _WORKSPACES[key] = buf
+    base = (buf.data_ptr() + 255) // 256 * 256
+    return ctypes.c_void_p(base), need.value
+
+
 def attention_packed(q: torch.Tensor, k_cache, v_cache, lo: int, hi: int, out: torch.Tensor | None = None,
                      softmax_scale: float | None = None, stats: torch.Tensor | None = None) -> torch.Tensor:
     """Fused int4-KV attention of q [B, Lq, H, D] bf16 over tokens [lo, hi) of two
@@ -229,7 +252,8 @@ def attention_packed(q: torch.Tensor, k_cache, v_cache, lo: int, hi: int, out: t
             float(softmax_scale) if softmax_scale else 0.0, _stream(dev))
     with torch.cuda.device(dev):
         if stats is None:
-            rc = _lib.load().kvq_attention(*common, *tail)
+            ws, wsb = _workspace(dev, B, Lq, H, int(hi) - int(lo))
+            rc = _lib.load().kvq_attention(*common, *tail[:-1], ws, wsb, tail[-1])
         else:
             _require_cuda(stats)
             if stats.dtype != torch.float32 or tuple(stats.shape) != (B, Lq, H, 4) or not stats.is_contiguous():
@@ -288,6 +312,7 @@ def attention_packed_gather(q: torch.Tensor, k_cache, v_cache, lo: int, hi: int,
     stride = out_heads * D if out_token_stride is None else int(out_token_stride)
     arr = (ctypes.c_void_p * len(outs))(*[ctypes.c_void_p(int(p)) for p in outs])
     cb = _host_map(k_cache.chan_band_host)
+    ws, wsb = _workspace(dev, B, Lq, H, int(hi) - int(lo))
     with torch.cuda.device(dev):
         rc = _lib.load().kvq_attention_gather(
             _ptr(q), q.stride(1), _ptr(k_cache.packed), _ptr(k_cache.scales), _ptr(k_cache.sink),
@@ -295,7 +320,7 @@ def attention_packed_gather(q: torch.Tensor, k_cache, v_cache, lo: int, hi: int,
             k_cache.sink_tokens if k_cache.sink is not None else 0, int(lo), int(hi),
             ctypes.cast(arr, ctypes.c_void_p), len(outs), int(out_head0), int(out_heads), stride,
             B, Lq, H, D, cb.ctypes.data_as(ctypes.c_void_p), len(k_cache.bands), k_cache.bits, v_cache.bits,
-            float(softmax_scale) if softmax_scale else 0.0, _stream(dev))
+            float(softmax_scale) if softmax_scale else 0.0, ws, wsb, _stream(dev))
     _lib.check(rc, "kvq_attention_gather")
 
 

