@@ -137,6 +137,30 @@ KVQ_API int kvq_attention_workspace_bytes(int batch, int64_t n_q, int n_heads, i
                                           int64_t* bytes);
 
 /*
+ * kvq_attention() for callers that cannot allocate device memory or hand over a
+ * workspace: a frame loop in which a cudaMalloc or cudaFree would synchronize the
+ * device and stall the frame, or a host framework that owns the device memory
+ * through its own pool and gives a plugin no way to ask for more. No counterpart
+ * in the reference (its attention is a library call with no workspace).
+ * The workspace is KVQ_NOALLOC_SCRATCH_BYTES of device memory inside the library,
+ * one instance per device; no call allocates. The first call on a device looks
+ * the scratch up (and loads the library's device code if that has not happened
+ * yet): make it before any stream capture. A shape whose workspace would be
+ * larger (kvq_attention_workspace_bytes) is rejected with KVQ_ERR_UNSUPPORTED.
+ * All calls on one device share the scratch: calls that may overlap on the GPU
+ * (streams not ordered with one another) race and corrupt each other's output.
+ * Arguments and results as kvq_attention() with a workspace.
+ */
+#define KVQ_NOALLOC_SCRATCH_BYTES (32ll << 20)
+KVQ_API int kvq_attention_noalloc(const void* q, int64_t q_token_stride,
+                                  const void* k_codes, const void* k_scales, const void* k_sink,
+                                  const void* v_codes, const void* v_scales, const void* v_sink,
+                                  int64_t cache_tokens, int64_t sink_tokens, int64_t lo, int64_t hi,
+                                  void* out, int64_t out_token_stride, int batch, int64_t n_q,
+                                  int n_heads, int head_dim, const int32_t* chan_band, int n_groups,
+                                  int k_bits, int v_bits, float softmax_scale, void* stream);
+
+/*
  * kvq_attention() that also writes, per (stream, query, head), four fp32 row
  * statistics of the attention distribution p = softmax(q k^T * scale) to
  * stats[batch][n_q][n_heads][4] (16-byte aligned): log-sum-exp of the scaled

@@ -1266,6 +1266,76 @@ extern "C" int kvq_attention_workspace_bytes(int batch, int64_t n_q, int n_heads
   return KVQ_OK;
 }
 
+// ------------------------------------------------------- no-allocation variant
+// Some callers cannot hand the launch a workspace: a frame loop in which a
+// cudaMalloc or cudaFree would synchronize the device and stall the frame, or a
+// host framework that owns the device memory through its own pool and gives a
+// plugin no way to ask for more. For them the wave-balance workspace lives in the
+// library itself: a fixed array in device memory, one instance per device, which
+// no call allocates. Calls on one device share it, so calls that may overlap on
+// the GPU (unordered streams) race; order them on one stream.
+static constexpr int64_t kNoAllocScratchBytes = KVQ_NOALLOC_SCRATCH_BYTES;
+static __device__ __align__(256) unsigned char g_attn_scratch[kNoAllocScratchBytes];
+
+// Device address of g_attn_scratch on the current device. The first call on a
+// device looks it up (cudaGetSymbolAddress, which loads the module if it is not
+// loaded yet); later calls read the cached address.
+static int noalloc_scratch(void** ptr) {
+  static std::mutex mu;
+  static void* addr[64];
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  KVQ_REQUIRE(e == cudaSuccess, KVQ_ERR_CUDA, "kvq_attention_noalloc: cudaGetDevice failed: %s",
+              cudaGetErrorString(e));
+  KVQ_REQUIRE(dev >= 0 && dev < 64, KVQ_ERR_DEVICE, "kvq_attention_noalloc: device %d out of range", dev);
+  std::lock_guard<std::mutex> g(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_attn_scratch);
+    KVQ_REQUIRE(e == cudaSuccess && p != nullptr, KVQ_ERR_CUDA,
+                "kvq_attention_noalloc: looking up the scratch on device %d failed: %s", dev,
+                cudaGetErrorString(e));
+    addr[dev] = p;
+  }
+  *ptr = addr[dev];
+  return KVQ_OK;
+}
+
+extern "C" int kvq_attention_noalloc(const void* q, int64_t q_token_stride, const void* k_codes,
+                                     const void* k_scales, const void* k_sink, const void* v_codes,
+                                     const void* v_scales, const void* v_sink, int64_t cache_tokens,
+                                     int64_t sink_tokens, int64_t lo, int64_t hi, void* out,
+                                     int64_t out_token_stride, int batch, int64_t n_q, int n_heads, int head_dim,
+                                     const int32_t* chan_band, int n_groups, int k_bits, int v_bits,
+                                     float softmax_scale, void* stream) {
+  clear_error();
+  int rc = require_sm100();
+  if (rc) return rc;
+  void* scratch = nullptr;
+  rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+  void* outs[1] = {out};
+  if (n_q > 0 && !out) {
+    set_error("NULL data pointer");
+    return KVQ_ERR_ARG;
+  }
+  // the shape checks attention_impl makes first, so that the plan below sees a sane shape
+  const bool planned = n_q > 0 && batch >= 1 && n_heads >= 1 && batch <= 65535 && n_heads <= 65535 &&
+                       n_q <= ((int64_t)1 << 30) && 0 <= lo && lo < hi &&
+                       (n_q + 2 * attn::BM - 1) / (2 * attn::BM) * n_heads * batch <= 0x7FFFFFFF;
+  if (planned) {
+    const int64_t need = attn::plan_split(n_q, n_heads * batch, hi - lo, attn::num_sms()).ws_bytes;
+    KVQ_REQUIRE(need <= kNoAllocScratchBytes, KVQ_ERR_UNSUPPORTED,
+                "kvq_attention_noalloc: this shape needs %lld bytes of scratch, more than the %lld the library "
+                "holds; call kvq_attention with a workspace of kvq_attention_workspace_bytes() bytes",
+                (long long)need, (long long)kNoAllocScratchBytes);
+  }
+  return attention_impl(q, q_token_stride, k_codes, k_scales, k_sink, v_codes, v_scales, v_sink, cache_tokens,
+                        sink_tokens, lo, hi, outs, 1, 0, n_heads, out_token_stride, batch, n_q, n_heads, head_dim,
+                        chan_band, n_groups, k_bits, v_bits, softmax_scale, stream, true, nullptr, sm100::kWaitCycles,
+                        -1, scratch, kNoAllocScratchBytes);
+}
+
 extern "C" int kvq_attention_stats(const void* q, int64_t q_token_stride, const void* k_codes,
                                    const void* k_scales, const void* k_sink, const void* v_codes,
                                    const void* v_scales, const void* v_sink, int64_t cache_tokens,

@@ -29,6 +29,8 @@ SIGNATURES = {
     "kvq_attention": (_i32, [_p, _i64, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _i64, _i32, _i64,
                              _i32, _i32, _p, _i32, _i32, _i32, _f32, _p, _i64, _p]),
     "kvq_attention_workspace_bytes": (_i32, [_i32, _i64, _i32, _i64, ctypes.POINTER(_i64)]),
+    "kvq_attention_noalloc": (_i32, [_p, _i64, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _i64, _i32,
+                                     _i64, _i32, _i32, _p, _i32, _i32, _i32, _f32, _p]),
     "kvq_attention_stats": (_i32, [_p, _i64, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _i64, _p, _i32,
                                    _i64, _i32, _i32, _p, _i32, _i32, _i32, _f32, _p]),
     "kvq_rope_quantize": (_i32, [_p, _i64, _p, _p, _p, _i64, _i64, _i32, _i32, _p, _i32, _i32, _p, _i32, _p, _p]),
