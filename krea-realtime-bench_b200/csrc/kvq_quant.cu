@@ -248,11 +248,10 @@ constexpr int pipe_smem_bytes() {
   return PipeCfg<BITS>::kStages * kQR * 256 + kQR * QuantConsts<BITS>::kCodeBytes + ((kQR * L::G * 2 + 15) / 16) * 16;
 }
 
-// Rotary embedding of one staged row in place (16 chunks of 4 bf16 pairs, XOR-
-// swizzled), as the upstream complex128 product (x0 + i x1)(cos + i sin) =
-// (x0 cos - x1 sin) + i (x0 sin + x1 cos), rounded to fp32 and then to bf16 (the
-// upstream result is float32 and the cache stores bf16). Products and sums are
-// separate IEEE fp64 operations. One chunk at a time keeps register use low.
+// Rotary embedding of one channel pair (two bf16 in one word) as the upstream
+// complex128 product (x0 + i x1)(cos + i sin) = (x0 cos - x1 sin) + i (x0 sin +
+// x1 cos), rounded to fp32 and then to bf16 (the upstream result is float32 and
+// the cache stores bf16). Products and sums are separate IEEE fp64 operations.
 __device__ __forceinline__ uint32_t rope_pair(uint32_t w, double2 cs) {
   const double x0 = static_cast<double>(__uint_as_float(w << 16));
   const double x1 = static_cast<double>(__uint_as_float(w & 0xFFFF0000u));
@@ -261,21 +260,48 @@ __device__ __forceinline__ uint32_t rope_pair(uint32_t w, double2 cs) {
   return pack_bf16x2(__double2float_rn(y0), __double2float_rn(y1));
 }
 
-__device__ __forceinline__ void rope_row(const QuantArgs& a, int64_t token, uint4* trow, int r) {
+// Rotary embedding of one staged row in place (16 chunks of 4 pairs, XOR-
+// swizzled), two chunks per step: the pairs of a step are independent
+// chains (two conversions to fp64, two products, a sum, a conversion back), so
+// more of them per step hide more of each chain's latency. The (cos, sin) loads
+// go through the read-only path and the stage through explicit shared-memory
+// accesses, so that the next step's loads are issued before this step's stores.
+constexpr int kRopeChunks = 2;
+__device__ __forceinline__ void rope_row(const QuantArgs& a, int64_t token, uint32_t trow, int r) {
+  constexpr int NP = 4 * kRopeChunks;  // pairs per step
   const int* pp = a.pos + token * 3;
-  const int p0 = min(max(pp[0], 0), a.max_pos - 1), p1 = min(max(pp[1], 0), a.max_pos - 1),
-            p2 = min(max(pp[2], 0), a.max_pos - 1);  // out-of-range positions clamp
-#pragma unroll 4
-  for (int c = 0; c < 16; ++c) {
-    uint4 v = trow[c ^ (r & 7)];
-    uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  const int p0 = min(max(__ldg(pp), 0), a.max_pos - 1), p1 = min(max(__ldg(pp + 1), 0), a.max_pos - 1),
+            p2 = min(max(__ldg(pp + 2), 0), a.max_pos - 1);  // out-of-range positions clamp
+  const double2* f0 = a.freqs + static_cast<int64_t>(p0) * 64;
+  const double2* f1 = a.freqs + static_cast<int64_t>(p1) * 64;
+  const double2* f2 = a.freqs + static_cast<int64_t>(p2) * 64;
+  auto fetch = [&](int i) { return __ldg((i < 22 ? f0 : (i < 43 ? f1 : f2)) + i); };
+  double2 cs[2][NP];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const int i = 4 * c + k;  // pair index = channels (2i, 2i+1)
-      const int p = i < 22 ? p0 : (i < 43 ? p1 : p2);
-      w[k] = rope_pair(w[k], a.freqs[static_cast<int64_t>(p) * 64 + i]);
+  for (int k = 0; k < NP; ++k) cs[0][k] = fetch(k);
+#pragma unroll
+  for (int st = 0; st < 64 / NP; ++st) {
+    if (st + 1 < 64 / NP) {
+#pragma unroll
+      for (int k = 0; k < NP; ++k) cs[(st + 1) & 1][k] = fetch(NP * (st + 1) + k);
     }
-    trow[c ^ (r & 7)] = make_uint4(w[0], w[1], w[2], w[3]);
+    uint32_t w[NP];
+#pragma unroll
+    for (int h = 0; h < kRopeChunks; ++h) {
+      const uint32_t addr = trow + (((kRopeChunks * st + h) ^ (r & 7)) << 4);
+      asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                   : "=r"(w[4 * h]), "=r"(w[4 * h + 1]), "=r"(w[4 * h + 2]), "=r"(w[4 * h + 3])
+                   : "r"(addr));
+    }
+#pragma unroll
+    for (int k = 0; k < NP; ++k) w[k] = rope_pair(w[k], cs[st & 1][k]);
+#pragma unroll
+    for (int h = 0; h < kRopeChunks; ++h) {
+      const uint32_t addr = trow + (((kRopeChunks * st + h) ^ (r & 7)) << 4);
+      asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(w[4 * h]), "r"(w[4 * h + 1]),
+                   "r"(w[4 * h + 2]), "r"(w[4 * h + 3])
+                   : "memory");
+    }
   }
 }
 
@@ -370,7 +396,7 @@ __global__ void __launch_bounds__(kQR, 3) quantize_rows_pipe(const __grid_consta
     if (tid < nrows) {
       // the rotated row replaces the staged input: the loads below, the exact-divide
       // fix-up and the sink copy all read the stage
-      if constexpr (ROPE) rope_row(a, (row0 + tid) / a.H, sm_in + stage * kQR * 16 + tid * 16, tid);
+      if constexpr (ROPE) rope_row(a, (row0 + tid) / a.H, in_base + ((stage * kQR + tid) * 16 << 4), tid);
       uint32_t w[64];
 #pragma unroll
       for (int c = 0; c < 16; ++c) {

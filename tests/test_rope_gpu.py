@@ -19,8 +19,8 @@ def _u16(t):
 @pytest.mark.parametrize("mode,bits", [("bands4", 4), ("bands", 4), ("blind64", 8)])
 @pytest.mark.parametrize("B,S,a,b,sink,t0,H", [(1, 4680, 0, 4680, 1560, 0, 5), (2, 3000, 1200, 2901, 1500, 9360, 5),
                                                (1, 500, 7, 8, 0, 77, 5),
-                                               # 16 heads or more: a 128-row tile spans at most 9 tokens; up to
-                                               # 8 tokens the (cos, sin) of the tile are gathered once
+                                               # 16-40 heads: a 128-row tile spans 4-9 tokens; 4680 x 40 rows
+                                               # are 1463 tiles, several per CTA
                                                (1, 4680, 0, 4680, 1560, 0, 40), (2, 1000, 33, 901, 100, 3120, 40),
                                                (1, 700, 5, 690, 64, 1560, 16), (1, 300, 0, 300, 0, 0, 18)])
 def test_rope_quantize_matches_oracle(mode, bits, B, S, a, b, sink, t0, H):
@@ -58,9 +58,8 @@ def test_rope_quantize_rejects_bad_arguments():
 
 def test_rope_quantize_special_values():
     """Zeros (both signs), subnormals and values near 2^126 (finite after the rotation) in the
-    keys before rotation take the exact widening path of the kernel; codes, scales
-    and sink rows stay bit-identical to the oracle (40 heads: the tile's (cos, sin)
-    come from shared memory)."""
+    keys before rotation: codes, scales and sink rows stay bit-identical to the
+    oracle."""
     import quant_kv
     from kvq import rope
     S, H = 600, 40
