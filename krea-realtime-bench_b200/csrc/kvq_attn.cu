@@ -474,26 +474,6 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
         l *= alpha;
       }
       if (STATS) mtrue = fmaxf(mtrue, mt);
-      if (__any_sync(0xffffffffu, rescale)) {
-        // O_x must hold every product up to PV_x(j-1) before it is rescaled:
-        // wait for S_x(j+1), issued behind PV_x(j-1) (the next commit into that
-        // buffer, S_x(j+3), follows PV_x(j+1), so the phase is unambiguous), or,
-        // at the last tile, for the commit that follows PV_x(j-1).
-        const bool last = j + 1 == nkv;
-        if (!mbar_wait_warp(&bars[last ? bOReady + x : bSFull + 2 * x + ((j + 1) & 1)],
-                            last ? 0u : static_cast<uint32_t>(((j + 1) >> 1) & 1), abort, &g_attn_status, lim))
-          return false;
-        tc_fence_after();
-#pragma unroll 1
-        for (int k = 0; k < 4; ++k) {
-          uint32_t o[32];
-          tmem_ld32_wait(tO + 32 * k, o);
-#pragma unroll
-          for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
-          tmem_st32(tO + 32 * k, o);
-        }
-        tmem_wait_st();
-      }
       const float nm = -m;
       float sum = 0.0f, sumb = 0.0f;
       uint32_t pw[32];
@@ -532,6 +512,29 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
           }
           ls += part;
         }
+      }
+      // The rescale of O comes after P: the tile's 64 logits are dead here (with
+      // them live, O's registers made the compiler spill). PV_x(j), which
+      // accumulates into the rescaled O, is issued only after this warp's arrival.
+      if (__any_sync(0xffffffffu, rescale)) {
+        // O_x must hold every product up to PV_x(j-1) before it is rescaled:
+        // wait for S_x(j+1), issued behind PV_x(j-1) (the next commit into that
+        // buffer, S_x(j+3), follows PV_x(j+1), so the phase is unambiguous), or,
+        // at the last tile, for the commit that follows PV_x(j-1).
+        const bool last = j + 1 == nkv;
+        if (!mbar_wait_warp(&bars[last ? bOReady + x : bSFull + 2 * x + ((j + 1) & 1)],
+                            last ? 0u : static_cast<uint32_t>(((j + 1) >> 1) & 1), abort, &g_attn_status, lim))
+          return false;
+        tc_fence_after();
+#pragma unroll 1
+        for (int k = 0; k < 8; ++k) {
+          uint32_t o[16];
+          tmem_ld16_wait(tO + 16 * k, o);
+#pragma unroll
+          for (int c = 0; c < 16; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+          tmem_st16(tO + 16 * k, o);
+        }
+        tmem_wait_st();
       }
       tmem_wait_st();  // P_x(j), 64 bf16 = 32 columns, over S_x(j)
       tc_fence_before();
