@@ -479,14 +479,18 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
       uint32_t pw[32];
       // P for tokens 0-31 of the tile (S columns 0-31) then 32-63: the first half's
       // TMEM store runs while the second half is computed
+      // paired f32x2 operations for the scaling and the row sum: half the issue
+      // slots of scalar ones, on sub-partitions shared with the converters
+      const float2 sc2 = make_float2(a.scale_log2, a.scale_log2), nm2 = make_float2(nm, nm);
+      float2 sum2 = make_float2(0.0f, 0.0f), sumb2 = make_float2(0.0f, 0.0f);
       auto half = [&](const uint32_t (&sv)[32], int base) {
 #pragma unroll
         for (int c = 0; c < 16; ++c) {
-          const float x0 = fmaf(__uint_as_float(sv[2 * c]), a.scale_log2, nm);
-          const float x1 = fmaf(__uint_as_float(sv[2 * c + 1]), a.scale_log2, nm);
-          const float p0 = ex2(x0), p1 = ex2(x1);
-          sum += p0 + p1;
-          if (STATS) sumb += p0 * x0 + p1 * x1;
+          const float2 xx =
+              __ffma2_rn(make_float2(__uint_as_float(sv[2 * c]), __uint_as_float(sv[2 * c + 1])), sc2, nm2);
+          const float p0 = ex2(xx.x), p1 = ex2(xx.y);
+          sum2 = __fadd2_rn(sum2, make_float2(p0, p1));
+          if (STATS) sumb2 = __ffma2_rn(make_float2(p0, p1), xx, sumb2);
           pw[base / 2 + c] = pack_bf16x2(p0, p1);
         }
       };
@@ -494,6 +498,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
       tmem_st16(tS, pw);
       half(s1, 32);
       tmem_st16(tS + 16, pw + 16);
+      sum = sum2.x + sum2.y;
+      if (STATS) sumb = sumb2.x + sumb2.y;
       l += sum;
       if (STATS) {
         lb += sumb;
