@@ -295,6 +295,10 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return d;
 }
 
+// Most parts a one-tile unit is cut into (at window 3 eight parts measured slower
+// than four: each part pays a CTA's fill and a partial store).
+constexpr int kMaxParts = 4;
+
 // Workspace slot (float4 [33][128] each) of Q tile x of part p of split unit u.
 __host__ __device__ __forceinline__ int64_t ws_slot(const Args& a, int u, int p, int x) {
   return u < a.split_full ? (static_cast<int64_t>(u) * 2 + p) * 2 + x
@@ -862,13 +866,13 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
         const float4* src = a.ws + ws_slot(a, unit, 0, x) * 33 * BM + r;
         // float4s from one part's slot to the next
         const int64_t pstride = (unit < a.split_full ? 2 : 1) * static_cast<int64_t>(33) * BM;
-        float wp[4];
+        float wp[kMaxParts];
         float mx = -INFINITY, L = 0.0f;
 #pragma unroll
-        for (int p = 0; p < 4; ++p)
+        for (int p = 0; p < kMaxParts; ++p)
           if (p < parts) mx = fmaxf(mx, __ldcg(src + p * pstride + 32 * BM).x);
 #pragma unroll
-        for (int p = 0; p < 4; ++p) {
+        for (int p = 0; p < kMaxParts; ++p) {
           wp[p] = 0.0f;
           if (p < parts) {
             const float4 ml = __ldcg(src + p * pstride + 32 * BM);
@@ -884,7 +888,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
 #pragma unroll
           for (int e = 0; e < 8; ++e) acc[e] = 0.0f;
 #pragma unroll
-          for (int p = 0; p < 4; ++p) {
+          for (int p = 0; p < kMaxParts; ++p) {
             if (p < parts) {
               const float4 v0 = __ldcg(src + p * pstride + (2 * ch) * BM);
               const float4 v1 = __ldcg(src + p * pstride + (2 * ch + 1) * BM);
@@ -1025,7 +1029,7 @@ static SplitPlan plan_split(int64_t n_q, int n_hb, int64_t n_kv, int sms) {
   const double base = makespan(n_ft, 0, n_s, 1, sms);
   double best = base;
   int best_k = 0, best_p = 1;
-  for (int P = 1; P <= 4 && P <= nkv; P *= 2) {
+  for (int P = 1; P <= kMaxParts && P <= nkv; P *= 2) {
     if (P > 1 && n_s == 0) break;
     for (int k = 0; k <= std::min(n_ft, 2 * sms); k += 4) {
       const double m = makespan(n_ft - k, k, n_s, P, sms);
