@@ -95,6 +95,23 @@ KVQ_API int kvq_dequantize(const void* codes, const void* scales, const void* si
                    const int32_t* chan_band, int n_groups, int bits, void* stream);
 
 /*
+ * The requantizing move of the reference's eviction `kv[:, a:b] = kv[:, c:d].clone()`
+ * (quant_kv.py:13; the clone dequantizes, quant_kv.py:189-199, and the slice write
+ * quantizes, quant_kv.py:201-215) in one pass over packed rows: for each of
+ * n_tokens x n_heads rows, value = the row's bf16 from src_exact for the first
+ * exact_tokens tokens (a source window's sink rows), else kvq_dequantize() of
+ * src_codes / src_scales; then dst_codes / dst_scales := kvq_quantize(value), and the
+ * first sink_tokens tokens' values also go to dst_sink. Bit-identical to
+ * kvq_dequantize() followed by kvq_quantize(), without the bf16 window in memory.
+ * int4 codes, head_dim 128 and the five specialised group maps (KVQ_ERR_UNSUPPORTED
+ * otherwise: take the two-call path). Source and destination must not overlap.
+ */
+KVQ_API int kvq_requantize(const void* src_codes, const void* src_scales, const void* src_exact,
+                           int64_t exact_tokens, void* dst_codes, void* dst_scales, void* dst_sink,
+                           int64_t sink_tokens, int64_t n_tokens, int n_heads, int head_dim,
+                           const int32_t* chan_band, int n_groups, int bits, void* stream);
+
+/*
  * Fused int4-KV attention over a cache window, reading K and V packed.
  * Replaces the read path `attention(q, kv_cache["k"][:, lo:hi], kv_cache["v"][:, lo:hi])`
  * (quant_kv.py:14): QuantKVTensor.__getitem__'s dequantize + bf16 sink overlay

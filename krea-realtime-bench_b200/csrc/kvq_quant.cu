@@ -305,19 +305,87 @@ __device__ __forceinline__ void rope_row(const QuantArgs& a, int64_t token, uint
   }
 }
 
+// One staged tile (kQR rows, XOR-swizzled in tin): thread tid < nrows quantizes
+// row tid into the codes / scales staging buffers; after a barrier of the CTA,
+// threads [0, kQR) store the tile's codes, scales and sink rows.
+template <class L, int BITS>
+__device__ __forceinline__ void quant_tile(const QuantArgs& a, int64_t row0, int nrows, const uint4* tin,
+                                           uint4* sm_codes, uint16_t* sm_sc, int tid) {
+  using C = QuantConsts<BITS>;
+  constexpr int G = L::G;
+  constexpr int CW = C::kCodeBytes;
+  constexpr int CCH = CW / 16;
+  if (tid < nrows) {
+    uint32_t w[64];
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+      uint4 v = tin[tid * 16 + (c ^ (tid & 7))];
+      w[4 * c + 0] = v.x;
+      w[4 * c + 1] = v.y;
+      w[4 * c + 2] = v.z;
+      w[4 * c + 3] = v.w;
+    }
+    uint32_t ow[BITS == 4 ? 16 : 32];
+#pragma unroll
+    for (int q = 0; q < (BITS == 4 ? 16 : 32); ++q) ow[q] = 0;
+    uint16_t sc[G];
+    uint32_t slow_mask = 0;
+    quant_row<L, BITS>(w, ow, sc, slow_mask, std::make_integer_sequence<int, G>{});
+#pragma unroll
+    for (int c = 0; c < CCH; ++c) {
+      const int slot = (BITS == 4) ? (c ^ ((tid >> 1) & 3)) : (c ^ (tid & 7));
+      sm_codes[tid * CCH + slot] = make_uint4(ow[4 * c], ow[4 * c + 1], ow[4 * c + 2], ow[4 * c + 3]);
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) sm_sc[tid * G + g] = sc[g];
+    if (slow_mask) {
+      int edges[G + 1];
+      fill_edges<L>(edges, std::make_integer_sequence<int, G + 1>{});
+      quant_fix_slow<BITS>(tin + tid * 16, tid, slow_mask, edges, sm_sc + tid * G, sm_codes + tid * CCH);
+    }
+  }
+  __syncthreads();
+  {
+    uint4* dst = reinterpret_cast<uint4*>(a.codes + row0 * CW);
+    for (int i = tid; i < nrows * CCH; i += kQR) {
+      const int r = i / CCH, c = i % CCH;
+      const int slot = (BITS == 4) ? (c ^ ((r >> 1) & 3)) : (c ^ (r & 7));
+      st_global_v4(dst + i, sm_codes[r * CCH + slot]);
+    }
+  }
+  {
+    uint16_t* dst = a.scales + row0 * G;
+    const int n = nrows * G;
+    if ((reinterpret_cast<uintptr_t>(dst) & 15) == 0 && (n % 8) == 0) {
+      const uint4* s4 = reinterpret_cast<const uint4*>(sm_sc);
+      for (int i = tid; i < n / 8; i += kQR) st_global_v4(reinterpret_cast<uint4*>(dst) + i, s4[i]);
+    } else if ((reinterpret_cast<uintptr_t>(dst) & 3) == 0 && (n % 2) == 0) {
+      const uint32_t* s2 = reinterpret_cast<const uint32_t*>(sm_sc);
+      for (int i = tid; i < n / 2; i += kQR) reinterpret_cast<uint32_t*>(dst)[i] = s2[i];
+    } else {
+      for (int i = tid; i < n; i += kQR) dst[i] = sm_sc[i];
+    }
+  }
+  if (a.sink != nullptr && row0 < a.sink_rows) {
+    const int ns = static_cast<int>(min(static_cast<int64_t>(nrows), a.sink_rows - row0));
+    uint4* dst = reinterpret_cast<uint4*>(a.sink + row0 * kQD);
+    for (int i = tid; i < ns * 16; i += kQR) {
+      const int r = i >> 4, c = i & 15;
+      st_global_v4(dst + i, tin[r * 16 + (c ^ (r & 7))]);
+    }
+  }
+}
+
 // Persistent CTAs walk the kQR-row tiles with a grid stride; each thread keeps
 // the next kStages-1 tiles' input in flight (cp.async, 16 bytes per copy, into
 // the XOR-swizzled layout) while it quantizes its row of the current tile.
 template <class L, int BITS, class P, bool ROPE>
 __global__ void __launch_bounds__(kQR, 3) quantize_rows_pipe(const __grid_constant__ P bt, int64_t n_tiles) {
-  using C = QuantConsts<BITS>;
-  constexpr int G = L::G;
   constexpr int S = PipeCfg<BITS>::kStages;
-  constexpr int CW = C::kCodeBytes;
-  constexpr int CCH = CW / 16;
+  constexpr int CW = QuantConsts<BITS>::kCodeBytes;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint4* sm_in = reinterpret_cast<uint4*>(smem_raw);                                   // S x kQR x 16 chunks
-  uint4* sm_codes = reinterpret_cast<uint4*>(smem_raw + S * kQR * 256);                // kQR x CCH
+  uint4* sm_codes = reinterpret_cast<uint4*>(smem_raw + S * kQR * 256);                // kQR x CW / 16
   uint16_t* sm_sc = reinterpret_cast<uint16_t*>(smem_raw + S * kQR * 256 + kQR * CW);  // kQR x G
   const int tid = threadIdx.x;
   const uint32_t in_base = static_cast<uint32_t>(__cvta_generic_to_shared(sm_in));
@@ -393,68 +461,12 @@ __global__ void __launch_bounds__(kQR, 3) quantize_rows_pipe(const __grid_consta
     const int64_t row0 = cl * kQR;
     advance(ci, cl);
     const int nrows = static_cast<int>(min(static_cast<int64_t>(kQR), a.n_rows - row0));
-    if (tid < nrows) {
-      // the rotated row replaces the staged input: the loads below, the exact-divide
-      // fix-up and the sink copy all read the stage
-      if constexpr (ROPE) rope_row(a, (row0 + tid) / a.H, in_base + ((stage * kQR + tid) * 16 << 4), tid);
-      uint32_t w[64];
-#pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        uint4 v = tin[tid * 16 + (c ^ (tid & 7))];
-        w[4 * c + 0] = v.x;
-        w[4 * c + 1] = v.y;
-        w[4 * c + 2] = v.z;
-        w[4 * c + 3] = v.w;
-      }
-      uint32_t ow[BITS == 4 ? 16 : 32];
-#pragma unroll
-      for (int q = 0; q < (BITS == 4 ? 16 : 32); ++q) ow[q] = 0;
-      uint16_t sc[G];
-      uint32_t slow_mask = 0;
-      quant_row<L, BITS>(w, ow, sc, slow_mask, std::make_integer_sequence<int, G>{});
-#pragma unroll
-      for (int c = 0; c < CCH; ++c) {
-        const int slot = (BITS == 4) ? (c ^ ((tid >> 1) & 3)) : (c ^ (tid & 7));
-        sm_codes[tid * CCH + slot] = make_uint4(ow[4 * c], ow[4 * c + 1], ow[4 * c + 2], ow[4 * c + 3]);
-      }
-#pragma unroll
-      for (int g = 0; g < G; ++g) sm_sc[tid * G + g] = sc[g];
-      if (slow_mask) {
-        int edges[G + 1];
-        fill_edges<L>(edges, std::make_integer_sequence<int, G + 1>{});
-        quant_fix_slow<BITS>(tin + tid * 16, tid, slow_mask, edges, sm_sc + tid * G, sm_codes + tid * CCH);
-      }
+    if constexpr (ROPE) {
+      // the rotated row replaces the staged input: the loads in quant_tile, the
+      // exact-divide fix-up and the sink copy all read the stage
+      if (tid < nrows) rope_row(a, (row0 + tid) / a.H, in_base + ((stage * kQR + tid) * 16 << 4), tid);
     }
-    __syncthreads();
-    {
-      uint4* dst = reinterpret_cast<uint4*>(a.codes + row0 * CW);
-      for (int i = tid; i < nrows * CCH; i += kQR) {
-        const int r = i / CCH, c = i % CCH;
-        const int slot = (BITS == 4) ? (c ^ ((r >> 1) & 3)) : (c ^ (r & 7));
-        st_global_v4(dst + i, sm_codes[r * CCH + slot]);
-      }
-    }
-    {
-      uint16_t* dst = a.scales + row0 * G;
-      const int n = nrows * G;
-      if ((reinterpret_cast<uintptr_t>(dst) & 15) == 0 && (n % 8) == 0) {
-        const uint4* s4 = reinterpret_cast<const uint4*>(sm_sc);
-        for (int i = tid; i < n / 8; i += kQR) st_global_v4(reinterpret_cast<uint4*>(dst) + i, s4[i]);
-      } else if ((reinterpret_cast<uintptr_t>(dst) & 3) == 0 && (n % 2) == 0) {
-        const uint32_t* s2 = reinterpret_cast<const uint32_t*>(sm_sc);
-        for (int i = tid; i < n / 2; i += kQR) reinterpret_cast<uint32_t*>(dst)[i] = s2[i];
-      } else {
-        for (int i = tid; i < n; i += kQR) dst[i] = sm_sc[i];
-      }
-    }
-    if (a.sink != nullptr && row0 < a.sink_rows) {
-      const int ns = static_cast<int>(min(static_cast<int64_t>(nrows), a.sink_rows - row0));
-      uint4* dst = reinterpret_cast<uint4*>(a.sink + row0 * kQD);
-      for (int i = tid; i < ns * 16; i += kQR) {
-        const int r = i >> 4, c = i & 15;
-        st_global_v4(dst + i, tin[r * 16 + (c ^ (r & 7))]);
-      }
-    }
+    quant_tile<L, BITS>(a, row0, nrows, tin, sm_codes, sm_sc, tid);
     __syncthreads();  // the stage and the staging buffers are reused by later tiles
   }
   cp_async_wait<0>();
@@ -778,6 +790,138 @@ static int dispatch_fast(int layout, const P& a, int64_t tiles, cudaStream_t st)
   return KVQ_ERR_UNSUPPORTED;
 }
 
+// ---------------------------------------------------------------- requantize
+// The requantizing move of the reference's eviction, kv[:, a:b] = kv[:, c:d].clone()
+// (quant_kv.py:13; the clone dequantizes, quant_kv.py:189-199, and the write
+// quantizes, quant_kv.py:201-215), in one pass over packed rows: each row is
+// dequantized into shared memory exactly as dequantize_rows_pipe does (or taken
+// from the source's bf16 rows below its sink), then quantized by quant_tile, which
+// also copies the first dst.sink_rows rows into the destination sink. Codes and
+// scales equal dequantize-then-quantize bit for bit; no bf16 window goes through
+// HBM (176 bytes per row instead of 688).
+struct RequantArgs {
+  DequantArgs src;  // codes, scales; sink / sink_rows = the source's bf16 rows below its sink
+  QuantArgs dst;    // codes, scales; sink / sink_rows = the destination's sink rows
+};
+
+template <class L>
+__global__ void __launch_bounds__(kQR, 3) requantize_rows_pipe(const __grid_constant__ RequantArgs ra,
+                                                               int64_t n_tiles) {
+  constexpr int G = L::G;
+  constexpr int CW = QuantConsts<4>::kCodeBytes;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint4* tin = reinterpret_cast<uint4*>(smem_raw);  // kQR x 16 chunks of bf16, XOR-swizzled
+  const uint32_t code_base = static_cast<uint32_t>(__cvta_generic_to_shared(smem_raw + kQR * 256));
+  const uint4* sm_code = reinterpret_cast<const uint4*>(smem_raw + kQR * 256);  // kDStages x kQR x 4 chunks
+  uint4* sm_codes = reinterpret_cast<uint4*>(smem_raw + kQR * 256 + kDStages * kQR * 64);  // kQR x CW / 16
+  uint16_t* sm_sc = reinterpret_cast<uint16_t*>(smem_raw + kQR * 256 + kDStages * kQR * 64 + kQR * CW);
+  const DequantArgs& a = ra.src;
+  const int tid = threadIdx.x;
+  pdl_wait();
+  pdl_launch_dependents();
+
+  auto issue = [&](int64_t tile, int stage) {
+    const int64_t row0 = tile * kQR;
+    const int nrows = static_cast<int>(min(static_cast<int64_t>(kQR), a.n_rows - row0));
+#pragma unroll
+    for (int i = tid; i < kQR * 4; i += kQR) {
+      const int r = i >> 2, c = i & 3;
+      if (r < nrows)
+        cp_async16(code_base + (((stage * kQR + r) * 4 + (c ^ ((r >> 1) & 3))) << 4), a.codes + (row0 + r) * 64 + c * 16);
+    }
+  };
+
+  const int64_t first = blockIdx.x;
+#pragma unroll
+  for (int s = 0; s < kDStages - 1; ++s) {
+    const int64_t t = first + static_cast<int64_t>(s) * gridDim.x;
+    if (t < n_tiles) issue(t, s);
+    cp_async_commit();
+  }
+  for (int64_t k = 0;; ++k) {
+    const int64_t tile = first + k * gridDim.x;
+    if (tile >= n_tiles) break;
+    const int64_t row0 = tile * kQR;
+    const int nrows = static_cast<int>(min(static_cast<int64_t>(kQR), a.n_rows - row0));
+    const int64_t row = row0 + tid;
+    const bool mine = tid < nrows;
+    const bool exact = mine && a.sink != nullptr && row < a.sink_rows;
+    // this row's scales (or bf16 row) are requested before waiting for the codes
+    uint32_t sp[G];
+    uint4 exact_row[16];
+    if (exact) {
+#pragma unroll
+      for (int c = 0; c < 16; ++c) exact_row[c] = ld_global_nc_v4(a.sink + row * kQD + c * 8);
+    } else if (mine) {
+      const uint16_t* srow = a.scales + row * G;
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const uint32_t v = __ldg(srow + g);
+        sp[g] = v | (v << 16);
+      }
+    }
+    {
+      const int64_t tn = tile + static_cast<int64_t>(kDStages - 1) * gridDim.x;
+      if (tn < n_tiles) issue(tn, static_cast<int>((k + kDStages - 1) % kDStages));
+      cp_async_commit();
+    }
+    cp_async_wait<kDStages - 1>();
+    __syncthreads();  // the tile's codes have landed; the previous tile's stage reads are done
+    const int stage = static_cast<int>(k % kDStages);
+    uint4* orow = tin + tid * 16;
+    if (exact) {
+#pragma unroll
+      for (int c = 0; c < 16; ++c) orow[c ^ (tid & 7)] = exact_row[c];
+    } else if (mine) {
+      uint32_t w[16];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const uint4 v = sm_code[(stage * kQR + tid) * 4 + (c ^ ((tid >> 1) & 3))];
+        w[4 * c] = v.x;
+        w[4 * c + 1] = v.y;
+        w[4 * c + 2] = v.z;
+        w[4 * c + 3] = v.w;
+      }
+      deq_row_to<L>(orow, tid, w, sp, std::make_integer_sequence<int, 16>{});
+    }
+    // quant_tile reads this thread's own row first, the other rows only after its barrier
+    quant_tile<L, 4>(ra.dst, row0, nrows, tin, sm_codes, sm_sc, tid);
+    __syncthreads();  // tin and the staging buffers are rewritten by the next tile
+  }
+  cp_async_wait<0>();
+}
+
+template <class L>
+constexpr int requant_smem_bytes() {
+  return kQR * 256 + kDStages * kQR * 64 + kQR * QuantConsts<4>::kCodeBytes + ((kQR * L::G * 2 + 15) / 16) * 16;
+}
+
+template <class L>
+static int launch_requant(const RequantArgs& ra, cudaStream_t st) {
+  constexpr int smem = requant_smem_bytes<L>();
+  static_assert(3 * (smem + 1024) <= 228 * 1024, "three CTAs per SM must fit");
+  static bool configured[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(requantize_rows_pipe<L>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) {
+      set_error("cudaFuncSetAttribute(requantize): %s", cudaGetErrorString(e));
+      return KVQ_ERR_CUDA;
+    }
+    configured[dev] = true;
+  }
+  const int64_t tiles = (ra.src.n_rows + kQR - 1) / kQR;
+  const int64_t cap = 3LL * num_sms();
+  cudaError_t e = launch_pdl(requantize_rows_pipe<L>, static_cast<unsigned>(tiles < cap ? tiles : cap), kQR, smem,
+                             st, ra, tiles);
+  if (e != cudaSuccess) {
+    set_error("kvq_requantize: launch failed: %s", cudaGetErrorString(e));
+    return KVQ_ERR_CUDA;
+  }
+  return check_launch("kvq_requantize");
+}
+
 template <class L>
 static int launch_dequant(const DequantArgs& a, cudaStream_t st) {
   constexpr int smem = kQT * 256 + kDStages * kQT * 64;
@@ -1004,4 +1148,60 @@ extern "C" int kvq_dequantize(const void* codes, const void* scales, const void*
   const int grid = static_cast<int>(blocks < num_sms() * 16 ? blocks : num_sms() * 16);
   dequantize_rows<<<grid, 256, 0, st>>>(a, map);
   return check_launch("kvq_dequantize");
+}
+
+extern "C" int kvq_requantize(const void* src_codes, const void* src_scales, const void* src_exact,
+                              int64_t exact_tokens, void* dst_codes, void* dst_scales, void* dst_sink,
+                              int64_t sink_tokens, int64_t n_tokens, int n_heads, int head_dim,
+                              const int32_t* chan_band, int n_groups, int bits, void* stream) {
+  clear_error();
+  KVQ_REQUIRE(n_tokens >= 0 && n_heads > 0, KVQ_ERR_ARG, "bad shape: n_tokens %lld, n_heads %d",
+              (long long)n_tokens, n_heads);
+  KVQ_REQUIRE(bits == 4 || bits == 8, KVQ_ERR_ARG, "bits must be 4 or 8, got %d", bits);
+  KVQ_REQUIRE(bits == 4 && head_dim == kQD, KVQ_ERR_UNSUPPORTED,
+              "the fused requantize is for int4 codes of head_dim %d (got %d bits, head_dim %d)", kQD, bits,
+              head_dim);
+  GroupMap map;
+  int layout = resolve_layout(chan_band, head_dim, n_groups, &map);
+  if (layout < 0) return layout;
+  KVQ_REQUIRE(layout != kLayoutGeneric, KVQ_ERR_UNSUPPORTED,
+              "the fused requantize supports the bands, bands2, bands4, blind32 and blind64 group maps");
+  KVQ_REQUIRE(exact_tokens >= 0 && sink_tokens >= 0, KVQ_ERR_ARG, "negative exact_tokens or sink_tokens");
+  KVQ_REQUIRE(exact_tokens == 0 || src_exact, KVQ_ERR_ARG, "exact_tokens > 0 needs src_exact");
+  KVQ_REQUIRE(sink_tokens == 0 || dst_sink, KVQ_ERR_ARG, "sink_tokens > 0 needs dst_sink");
+  if (n_tokens == 0) return KVQ_OK;
+  KVQ_REQUIRE(src_codes && src_scales && dst_codes && dst_scales, KVQ_ERR_ARG, "NULL data pointer");
+  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  KVQ_REQUIRE(al16(src_codes) && al16(dst_codes), KVQ_ERR_ALIGN, "codes must be 16-byte aligned");
+  KVQ_REQUIRE((reinterpret_cast<uintptr_t>(src_scales) & 1) == 0 && (reinterpret_cast<uintptr_t>(dst_scales) & 1) == 0,
+              KVQ_ERR_ALIGN, "scales must be 2-byte aligned");
+  KVQ_REQUIRE((exact_tokens == 0 || al16(src_exact)) && (sink_tokens == 0 || al16(dst_sink)), KVQ_ERR_ALIGN,
+              "src_exact and dst_sink must be 16-byte aligned");
+  int rc = require_sm100();
+  if (rc) return rc;
+  RequantArgs ra;
+  memset(&ra, 0, sizeof(ra));
+  ra.src.codes = static_cast<const uint8_t*>(src_codes);
+  ra.src.scales = static_cast<const uint16_t*>(src_scales);
+  ra.src.sink = exact_tokens > 0 ? static_cast<const uint16_t*>(src_exact) : nullptr;
+  ra.src.sink_rows = (exact_tokens < n_tokens ? exact_tokens : n_tokens) * n_heads;
+  ra.src.n_rows = n_tokens * n_heads;
+  ra.src.H = n_heads;
+  ra.src.D = head_dim;
+  ra.src.G = n_groups;
+  ra.src.bits = bits;
+  ra.src.rows_contig = 1;
+  ra.dst = quant_args(nullptr, static_cast<int64_t>(n_heads) * head_dim, dst_codes, dst_scales,
+                      sink_tokens > 0 ? dst_sink : nullptr, sink_tokens, n_tokens, n_heads, head_dim);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (layout) {
+    case kLayoutBands: return launch_requant<LayoutBands>(ra, st);
+    case kLayoutBands2: return launch_requant<LayoutBands2>(ra, st);
+    case kLayoutBands4: return launch_requant<LayoutBands4>(ra, st);
+    case kLayoutBlind32: return launch_requant<LayoutBlind32>(ra, st);
+    case kLayoutBlind64: return launch_requant<LayoutBlind64>(ra, st);
+    default: break;
+  }
+  set_error("internal: unhandled layout %d", layout);
+  return KVQ_ERR_UNSUPPORTED;
 }

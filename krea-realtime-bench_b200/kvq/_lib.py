@@ -26,6 +26,7 @@ SIGNATURES = {
     "kvq_last_error": (ctypes.c_char_p, []),
     "kvq_quantize": (_i32, [_p, _i64, _p, _p, _p, _i64, _i64, _i32, _i32, _p, _i32, _i32, _p]),
     "kvq_dequantize": (_i32, [_p, _p, _p, _i64, _p, _i64, _i64, _i32, _i32, _p, _i32, _i32, _p]),
+    "kvq_requantize": (_i32, [_p, _p, _p, _i64, _p, _p, _p, _i64, _i64, _i32, _i32, _p, _i32, _i32, _p]),
     "kvq_attention": (_i32, [_p, _i64, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _i64, _i32, _i64,
                              _i32, _i32, _p, _i32, _i32, _i32, _f32, _p, _i64, _p]),
     "kvq_attention_workspace_bytes": (_i32, [_i32, _i64, _i32, _i64, ctypes.POINTER(_i64)]),

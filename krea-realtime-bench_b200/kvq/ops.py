@@ -198,6 +198,42 @@ def dequantize_into(codes: torch.Tensor, scales: torch.Tensor, out: torch.Tensor
     return out
 
 
+def requantize_into(src_codes: torch.Tensor, src_scales: torch.Tensor, dst_codes: torch.Tensor,
+                    dst_scales: torch.Tensor, chan_band, n_groups: int, bits: int = 4,
+                    exact: torch.Tensor | None = None, exact_tokens: int = 0,
+                    sink: torch.Tensor | None = None, sink_tokens: int = 0) -> bool:
+    """dst := quantize(dequantize(src)) for packed rows [L, H, *] (kvq_requantize):
+    the first exact_tokens source tokens take their bf16 rows from `exact` instead
+    of their codes, and the first sink_tokens destination tokens also get the bf16
+    rows in `sink`. Returns False, launching nothing, when the fused kernel does not
+    cover the format (int8 codes, head_dim other than 128, a generic group map)."""
+    dev = _require_cuda(src_codes, src_scales, dst_codes, dst_scales, exact, sink)
+    L, H, cw = src_codes.shape
+    D = 2 * cw if bits == 4 else cw
+    for name, t, shape, dt in (("src_codes", src_codes, (L, H, cw), torch.uint8),
+                               ("dst_codes", dst_codes, (L, H, cw), torch.uint8),
+                               ("src_scales", src_scales, (L, H, n_groups), torch.bfloat16),
+                               ("dst_scales", dst_scales, (L, H, n_groups), torch.bfloat16)):
+        if t.dtype != dt or tuple(t.shape) != shape or not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous {dt} {shape}, got {t.dtype} {tuple(t.shape)}")
+    for name, t, n in (("exact", exact, exact_tokens), ("sink", sink, sink_tokens)):
+        if t is not None and (t.dtype != torch.bfloat16 or not t.is_contiguous()
+                              or tuple(t.shape[1:]) != (H, D) or t.shape[0] < min(n, L)):
+            raise ValueError(f"{name} must be contiguous bf16 [>={name}_tokens, H, D]")
+    cb = _host_map(chan_band)
+    if cb.shape[0] != D:
+        raise ValueError(f"chan_band has {cb.shape[0]} entries, head_dim is {D}")
+    with torch.cuda.device(dev):
+        rc = _lib.load().kvq_requantize(
+            _ptr(src_codes), _ptr(src_scales), _ptr(exact), int(exact_tokens) if exact is not None else 0,
+            _ptr(dst_codes), _ptr(dst_scales), _ptr(sink), int(sink_tokens) if sink is not None else 0,
+            L, H, D, cb.ctypes.data_as(ctypes.c_void_p), int(n_groups), int(bits), _stream(dev))
+    if rc == _lib.KVQ_ERR_UNSUPPORTED:
+        return False
+    _lib.check(rc, "kvq_requantize")
+    return True
+
+
 # Per (device, stream) workspace of the attention launches (kvq_attention's
 # wave-balance parts): grown when a launch needs more, reused in stream order.
 _WORKSPACES: dict = {}

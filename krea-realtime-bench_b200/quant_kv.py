@@ -16,8 +16,12 @@ Behaviour a caller can see, against the reference:
     temporary + copy), codes/scales bit-exact to the reference torch path;
   * slice reads `t[:, a:b]` return a QuantKVWindow, a lazy view of the packed
     window. attention() reads it in packed form; any other use (a torch
-    function, a tensor method, `.clone()`) dequantizes it exactly as the
-    reference's __getitem__ does (quant_kv.py:189-199), sink overlay included;
+    function, a tensor method) dequantizes it exactly as the reference's
+    __getitem__ does (quant_kv.py:189-199), sink overlay included;
+  * `t[:, a:b].clone()` is a packed snapshot (PackedBlock) with the same bf16
+    values as the reference's clone; written into a slice (the eviction
+    `kv[:, a:b] = kv[:, c:d].clone()`, quant_kv.py:13) it is requantized in one
+    fused pass, bit-exact to the reference's dequantize + quantize;
   * the leading dimension may be > 1: independent streams, each with its own
     window (the reference asserts batch 1, quant_kv.py:95);
   * there is no CPU path (the reference falls back to torch on CPU,
@@ -234,9 +238,12 @@ class QuantKVTensor:
         a, b, _ = sl.indices(self.n_tokens)
         if b <= a:
             return
-        if isinstance(value, PackedBlock) and self.lossless_moves and value.fits(self, b - a):
-            self.write_packed_(a, b, value)
-            return
+        if isinstance(value, PackedBlock) and value.fits(self, b - a):
+            if self.lossless_moves:
+                self.write_packed_(a, b, value)
+                return
+            if self.write_requant_(a, b, value):
+                return
         if isinstance(value, QuantKVWindow):
             value = value.materialize()
         self.write_(a, b, value)
@@ -254,6 +261,30 @@ class QuantKVTensor:
             self.scales[rows].copy_(blk.scales[i * L:(i + 1) * L])
             if ns > 0:
                 self.sink[self._sink_rows(i, a, a + ns)].copy_(blk.read_rows(i, 0, ns))
+
+    def write_requant_(self, a, b, blk) -> bool:
+        """Tokens [a, b) := quantize(blk's bf16 read), as the reference's slice write of
+        a cloned window does (quant_kv.py:13, 201-215), in one fused pass over blk's
+        packed rows (kvq_requantize): no bf16 window is materialized. Destination
+        tokens below sink_tokens also get the bf16 values in the sink. Returns False,
+        writing nothing, for a format the fused kernel does not cover."""
+        L = b - a
+        if self.bits != 4 or self.head_dim != 128:
+            return False
+        ns = max(0, min(b, self.sink_tokens) - a) if self.sink is not None else 0
+        for i in range(self.n_streams):
+            rows = self._rows(i, a, b)
+            exact = blk.exact[i] if blk.n_exact > 0 else None
+            sink = self.sink[self._sink_rows(i, a, a + ns)] if ns > 0 else None
+            done = _ops.requantize_into(blk.packed[i * L:(i + 1) * L], blk.scales[i * L:(i + 1) * L],
+                                        self.packed[rows], self.scales[rows], self.chan_band_host,
+                                        len(self.bands), self.bits, exact=exact, exact_tokens=blk.n_exact,
+                                        sink=sink, sink_tokens=ns)
+            if not done:
+                assert i == 0, "the fused requantize covers every stream of a cache or none"
+                return False
+            self.version += 1
+        return True
 
     def clone(self):
         raise RuntimeError("QuantKVTensor.clone(): the runtime only clones windows (t[:, a:b].clone()); "
@@ -364,14 +395,16 @@ class QuantKVWindow:
     attention() consumes it packed. Everything else sees the dequantized bf16
     window of the reference's __getitem__ (quant_kv.py:189-199), materialized on
     use: torch functions (via __torch_function__), tensor methods and
-    attributes (delegated), arithmetic operators and `.clone()`.
+    attributes (delegated) and arithmetic operators; `.clone()` takes a packed
+    snapshot (PackedBlock) of the same values.
 
     One difference to the reference, whose __getitem__ returns a snapshot: the
     window is read when it is used, not when it is taken. So that this can never
     return newer data silently, a window refuses to be used (RuntimeError) once
     its cache has been written after the window was taken; take the window
-    again, or `.clone()` it before the write to keep the old contents. The
-    runtime's three patterns (quant_kv.py:12-14) always use a window at once.
+    again, or `.clone()` it before the write to keep the old contents (the clone
+    is a packed snapshot, PackedBlock). The runtime's three patterns
+    (quant_kv.py:12-14) always use a window at once.
     """
 
     def __init__(self, cache: QuantKVTensor, lo: int, hi: int):
@@ -408,12 +441,12 @@ class QuantKVWindow:
 
     def clone(self, *a, **kw):
         # the runtime's eviction `kv[:, a:b] = kv[:, c:d].clone()` (quant_kv.py:13): the
-        # reference dequantizes here and requantizes on the write (quant_kv.py:217-218);
-        # with lossless_moves the clone keeps the packed rows instead
-        if self.cache.lossless_moves:
-            self.check_fresh()
-            return PackedBlock(self.cache, self.lo, self.hi)
-        return self.materialize()
+        # reference dequantizes here and requantizes on the write (quant_kv.py:217-218).
+        # The clone is a packed snapshot of the window; written into a cache slice it
+        # is requantized in one fused pass (or, with lossless_moves, copied as it is),
+        # and any other use sees the same bf16 values as the reference's clone.
+        self.check_fresh()
+        return PackedBlock(self.cache, self.lo, self.hi)
 
     @classmethod
     def __torch_function__(cls, func, types, args=(), kwargs=None):
@@ -440,9 +473,11 @@ class QuantKVWindow:
 class PackedBlock(QuantKVWindow):
     """Snapshot of tokens [lo, hi) of a QuantKVTensor in packed form (codes,
     scales, and the bf16 sink rows the window overlaps), made by clone() of a
-    window of a cache with lossless_moves. Writing it into a slice of a cache of
-    the same format copies the packed rows unchanged; any other use sees the
-    window's bf16 read (dequantize + sink overlay) as of the snapshot."""
+    window. Writing it into a slice of a cache of the same format requantizes its
+    bf16 read in one fused pass, as the reference's write of the dequantized clone
+    does (with lossless_moves: copies the packed rows unchanged); any other use sees
+    the window's bf16 read (dequantize + sink overlay) as of the snapshot, which is
+    what the reference's clone holds. Unlike that clone it is not a torch.Tensor."""
 
     def __init__(self, cache: QuantKVTensor, lo: int, hi: int):
         super().__init__(cache, lo, hi)

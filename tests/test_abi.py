@@ -81,6 +81,25 @@ def test_dequantize_rejects_bad_arguments_without_launching(libkvq):
     assert rc == -4
 
 
+def test_requantize_rejects_bad_arguments_without_launching(libkvq):
+    cb = _cb()
+    p = ctypes.c_void_p(16)
+    cbp = cb.ctypes.data_as(ctypes.c_void_p)
+    # int8 codes and a generic group map are not covered by the fused kernel
+    assert libkvq.kvq_requantize(p, p, None, 0, p, p, None, 0, 4, 40, 128, cbp, 3, 8, None) == -2
+    blind16 = np.repeat(np.arange(8, dtype=np.int32), 16)
+    assert libkvq.kvq_requantize(p, p, None, 0, p, p, None, 0, 4, 40, 128,
+                                 blind16.ctypes.data_as(ctypes.c_void_p), 8, 4, None) == -2
+    # exact tokens without their bf16 rows, sink tokens without a sink
+    assert libkvq.kvq_requantize(p, p, None, 5, p, p, None, 0, 4, 40, 128, cbp, 3, 4, None) == -1
+    assert libkvq.kvq_requantize(p, p, None, 0, p, p, None, 5, 4, 40, 128, cbp, 3, 4, None) == -1
+    # misaligned destination codes
+    rc = libkvq.kvq_requantize(p, p, None, 0, ctypes.c_void_p(24), p, None, 0, 4, 40, 128, cbp, 3, 4, None)
+    assert rc == -4 and b"aligned" in libkvq.kvq_last_error()
+    # zero tokens is a no-op success
+    assert libkvq.kvq_requantize(p, p, None, 0, p, p, None, 0, 0, 40, 128, cbp, 3, 4, None) == 0
+
+
 def test_python_error_mapping(libkvq):
     from kvq import _lib
     cb = _cb()

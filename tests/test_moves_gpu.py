@@ -2,7 +2,8 @@
 runtime's `kv[:, a:b] = kv[:, c:d].clone()` copies codes and scales unchanged,
 so the destination reads back exactly what the source read before the move;
 overlapping ranges behave like memmove; destination rows inside the sink get the
-source's read values; the default keeps the reference's dequantize-requantize."""
+source's read values. The default keeps the reference's dequantize-requantize,
+as one fused pass over the packed snapshot (kvq_requantize)."""
 import pytest
 import torch
 
@@ -59,20 +60,52 @@ def test_lossless_move_reads_back_exactly(B, S, sink, src, dst):
 
 
 def test_default_keeps_requantizing_semantics():
-    """Without the flag the clone is the bf16 read and the write requantizes it,
+    """Without the flag the clone holds the bf16 read and the write requantizes it,
     exactly as writing that tensor would (the reference's path)."""
     import quant_kv
     c = _cache(1, 3000, 4, 500, False)
     _fill(c, seed=7)
     v = c[:, 1500:2500].clone()
-    assert isinstance(v, torch.Tensor)
+    assert isinstance(v, quant_kv.PackedBlock)
     ref = _cache(1, 3000, 4, 500, False)
     _fill(ref, seed=7)
     c[:, 500:1500] = v
-    ref[:, 500:1500] = v.clone()
+    ref[:, 500:1500] = v.materialize()
     assert torch.equal(c.packed, ref.packed)
     assert torch.equal(_bits(c.scales), _bits(ref.scales))
     assert torch.equal(_bits(c.sink), _bits(ref.sink))
+
+
+@pytest.mark.parametrize("mode,bits", [("bands4", 4), ("bands", 4), ("blind64", 4), ("bands4", 8)])
+@pytest.mark.parametrize("B,S,H,sink,src,dst", [
+    (1, 4000, 4, 1000, (2000, 3500), (1000, 2500)),       # eviction after the sink, overlapping
+    (2, 3000, 4, 500, (1200, 1900), (1500, 2200)),        # overlapping, moving up
+    (1, 2000, 4, 600, (100, 400), (900, 1200)),           # sink rows (exact) to outside the sink
+    (2, 2000, 4, 600, (1300, 1700), (400, 800)),          # outside rows into the sink border
+    (1, 300, 3, 0, (77, 211), (0, 134)),                  # ragged, no sink
+    (1, 32760, 40, 1560, (6240, 32760), (1560, 28080)),   # the window-21 eviction of one block
+])
+def test_requantizing_move_equals_two_pass(mode, bits, B, S, H, sink, src, dst):
+    """The default eviction `kv[:, a:b] = kv[:, c:d].clone()`: the write of the
+    packed snapshot (one fused kvq_requantize pass for int4; the dequantize +
+    quantize pair otherwise) equals quantizing the window's bf16 read, codes,
+    scales and sink rows bit for bit."""
+    import quant_kv
+    if S > 10000 and (mode, bits) != ("bands4", 4):
+        pytest.skip("the window-21 shape runs for the default format only")
+    c = _cache(B, S, H, sink, False, mode, bits)
+    ref = _cache(B, S, H, sink, False, mode, bits)
+    for t in (c, ref):
+        _fill(t, seed=B * 100 + S + H)
+    blk = c[:, src[0]:src[1]].clone()
+    assert isinstance(blk, quant_kv.PackedBlock)
+    values = ref[:, src[0]:src[1]].materialize()
+    c[:, dst[0]:dst[1]] = blk
+    ref.write_(dst[0], dst[1], values)
+    assert torch.equal(c.packed, ref.packed)
+    assert torch.equal(_bits(c.scales), _bits(ref.scales))
+    if sink:
+        assert torch.equal(_bits(c.sink), _bits(ref.sink))
 
 
 def test_packed_block_behaves_like_its_read():
