@@ -941,6 +941,14 @@ def run_profile_case(case: str, launches: int = 6):
             ops.quantize_layers_into(xs, cs, ss, cb, G, 4)
             ops.rope_quantize_into(xs[0], cs[0], ss[0], cb, G, 4, fr, pos)
             ops.dequantize_into(cs[1], ss[1], xs[1], cb, G, 4)
+    elif case == "requantize":
+        # the window-21 eviction of one block after the 1560-token sink in one layer
+        # tensor, through the public API: a packed snapshot copy + one kvq_requantize
+        S = 21 * FRAME
+        c = quant_kv.QuantKVTensor([1, S, H_TOTAL, D], dev, torch.bfloat16, 4, MODE, SINK)
+        c[:, 0:S] = synth.make_k(S, H_TOTAL, seed=5, device=dev).unsqueeze(0)
+        for _ in range(launches):
+            c[:, SINK:S - FRAME * 3] = c[:, SINK + FRAME * 3:S].clone()
     else:
         bands = quant_kv._band_edges(D, MODE)
         G = len(bands)
@@ -971,7 +979,7 @@ def main():
     ap.add_argument("--gather", default="fused", choices=("fused", "nccl"),
                     help="N > 1: all-gather of the output in the attention epilogue, or by NCCL")
     ap.add_argument("--profile-case", choices=("attention", "attention_gather", "attention_stats", "quantize",
-                                               "dequantize", "append", "rope"),
+                                               "dequantize", "append", "rope", "requantize"),
                     help="run a few launches of one kernel for an ncu capture and exit")
     args = ap.parse_args()
     if args.profile_case:
