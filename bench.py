@@ -350,6 +350,9 @@ def run_ours(args):
     t_ms = max_over_ranks(e0.elapsed_time(e1), world, dev)
     k_ms = [a.elapsed_time(b) for a, b in kevs]
     k_mean = sum(k_ms) / len(k_ms)
+    # per-rank attention time at N > 1 (the step also waits for the slowest rank)
+    k_max_ranks = max_over_ranks(k_mean, world, dev)
+    k_min_ranks = -max_over_ranks(-k_mean, world, dev)
     status = ops.device_status()
     if status != 0:
         raise SystemExit(f"device status {status}: a kernel wait timed out; results invalid")
@@ -388,6 +391,7 @@ def run_ours(args):
                      "traffic": traffic,
                      "kernel": "attention_kernel (tcgen05, per-launch CUDA events, mean)",
                      "kernel_ms": k_mean,
+                     "kernel_ms_over_ranks": {"min": k_min_ranks, "max": k_max_ranks},
                      "peak_source": f"{peaks['source']} bf16 dense (burst), of {peaks['source']}"},
         "e2e": e2e,
         "gpu_launches": args.steps * (2 if fused else 1),

@@ -804,17 +804,17 @@ struct RequantArgs {
   QuantArgs dst;    // codes, scales; sink / sink_rows = the destination's sink rows
 };
 
+constexpr int kRStages = 2;  // code stages of the requantize kernel (one tile in flight)
+
 template <class L>
-__global__ void __launch_bounds__(kQR, 3) requantize_rows_pipe(const __grid_constant__ RequantArgs ra,
+__global__ void __launch_bounds__(kQR, 4) requantize_rows_pipe(const __grid_constant__ RequantArgs ra,
                                                                int64_t n_tiles) {
   constexpr int G = L::G;
-  constexpr int CW = QuantConsts<4>::kCodeBytes;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint4* tin = reinterpret_cast<uint4*>(smem_raw);  // kQR x 16 chunks of bf16, XOR-swizzled
   const uint32_t code_base = static_cast<uint32_t>(__cvta_generic_to_shared(smem_raw + kQR * 256));
-  const uint4* sm_code = reinterpret_cast<const uint4*>(smem_raw + kQR * 256);  // kDStages x kQR x 4 chunks
-  uint4* sm_codes = reinterpret_cast<uint4*>(smem_raw + kQR * 256 + kDStages * kQR * 64);  // kQR x CW / 16
-  uint16_t* sm_sc = reinterpret_cast<uint16_t*>(smem_raw + kQR * 256 + kDStages * kQR * 64 + kQR * CW);
+  uint4* sm_code = reinterpret_cast<uint4*>(smem_raw + kQR * 256);  // kRStages x kQR x 4 chunks
+  uint16_t* sm_sc = reinterpret_cast<uint16_t*>(smem_raw + kQR * 256 + kRStages * kQR * 64);
   const DequantArgs& a = ra.src;
   const int tid = threadIdx.x;
   pdl_wait();
@@ -832,12 +832,8 @@ __global__ void __launch_bounds__(kQR, 3) requantize_rows_pipe(const __grid_cons
   };
 
   const int64_t first = blockIdx.x;
-#pragma unroll
-  for (int s = 0; s < kDStages - 1; ++s) {
-    const int64_t t = first + static_cast<int64_t>(s) * gridDim.x;
-    if (t < n_tiles) issue(t, s);
-    cp_async_commit();
-  }
+  if (first < n_tiles) issue(first, 0);
+  cp_async_commit();
   for (int64_t k = 0;; ++k) {
     const int64_t tile = first + k * gridDim.x;
     if (tile >= n_tiles) break;
@@ -846,13 +842,9 @@ __global__ void __launch_bounds__(kQR, 3) requantize_rows_pipe(const __grid_cons
     const int64_t row = row0 + tid;
     const bool mine = tid < nrows;
     const bool exact = mine && a.sink != nullptr && row < a.sink_rows;
-    // this row's scales (or bf16 row) are requested before waiting for the codes
+    // this row's scales are requested before waiting for the codes
     uint32_t sp[G];
-    uint4 exact_row[16];
-    if (exact) {
-#pragma unroll
-      for (int c = 0; c < 16; ++c) exact_row[c] = ld_global_nc_v4(a.sink + row * kQD + c * 8);
-    } else if (mine) {
+    if (mine && !exact) {
       const uint16_t* srow = a.scales + row * G;
 #pragma unroll
       for (int g = 0; g < G; ++g) {
@@ -861,17 +853,17 @@ __global__ void __launch_bounds__(kQR, 3) requantize_rows_pipe(const __grid_cons
       }
     }
     {
-      const int64_t tn = tile + static_cast<int64_t>(kDStages - 1) * gridDim.x;
-      if (tn < n_tiles) issue(tn, static_cast<int>((k + kDStages - 1) % kDStages));
+      const int64_t tn = tile + gridDim.x;
+      if (tn < n_tiles) issue(tn, static_cast<int>((k + 1) % kRStages));
       cp_async_commit();
     }
-    cp_async_wait<kDStages - 1>();
+    cp_async_wait<1>();
     __syncthreads();  // the tile's codes have landed; the previous tile's stage reads are done
-    const int stage = static_cast<int>(k % kDStages);
+    const int stage = static_cast<int>(k % kRStages);
     uint4* orow = tin + tid * 16;
     if (exact) {
 #pragma unroll
-      for (int c = 0; c < 16; ++c) orow[c ^ (tid & 7)] = exact_row[c];
+      for (int c = 0; c < 16; ++c) orow[c ^ (tid & 7)] = ld_global_nc_v4(a.sink + row * kQD + c * 8);
     } else if (mine) {
       uint32_t w[16];
 #pragma unroll
@@ -884,8 +876,10 @@ __global__ void __launch_bounds__(kQR, 3) requantize_rows_pipe(const __grid_cons
       }
       deq_row_to<L>(orow, tid, w, sp, std::make_integer_sequence<int, 16>{});
     }
-    // quant_tile reads this thread's own row first, the other rows only after its barrier
-    quant_tile<L, 4>(ra.dst, row0, nrows, tin, sm_codes, sm_sc, tid);
+    // The tile's code stage doubles as the codes staging buffer: each thread has
+    // read its own row's codes above and quant_tile writes that row's new codes
+    // over them (same 64 bytes, same swizzle) before its barrier.
+    quant_tile<L, 4>(ra.dst, row0, nrows, tin, sm_code + stage * kQR * 4, sm_sc, tid);
     __syncthreads();  // tin and the staging buffers are rewritten by the next tile
   }
   cp_async_wait<0>();
@@ -893,13 +887,13 @@ __global__ void __launch_bounds__(kQR, 3) requantize_rows_pipe(const __grid_cons
 
 template <class L>
 constexpr int requant_smem_bytes() {
-  return kQR * 256 + kDStages * kQR * 64 + kQR * QuantConsts<4>::kCodeBytes + ((kQR * L::G * 2 + 15) / 16) * 16;
+  return kQR * 256 + kRStages * kQR * 64 + ((kQR * L::G * 2 + 15) / 16) * 16;
 }
 
 template <class L>
 static int launch_requant(const RequantArgs& ra, cudaStream_t st) {
   constexpr int smem = requant_smem_bytes<L>();
-  static_assert(3 * (smem + 1024) <= 228 * 1024, "three CTAs per SM must fit");
+  static_assert(4 * (smem + 1024) <= 228 * 1024, "four CTAs per SM must fit");
   static bool configured[64];
   int dev = 0;
   cudaGetDevice(&dev);
@@ -912,7 +906,7 @@ static int launch_requant(const RequantArgs& ra, cudaStream_t st) {
     configured[dev] = true;
   }
   const int64_t tiles = (ra.src.n_rows + kQR - 1) / kQR;
-  const int64_t cap = 3LL * num_sms();
+  const int64_t cap = 4LL * num_sms();
   cudaError_t e = launch_pdl(requantize_rows_pipe<L>, static_cast<unsigned>(tiles < cap ? tiles : cap), kQR, smem,
                              st, ra, tiles);
   if (e != cudaSuccess) {
