@@ -612,7 +612,10 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
         if (lane == 0) mbar_arrive(&bars[bEpi + x]);
         if ((warp & 3) == 0 && lane == 0 && mbar_wait(&bars[bEpi + x], 0, abort, &g_attn_status, lim)) {
           const int xq = (a.out_head0 + h) * D, yq = q0 + x * BM;
-          for (int d = 0; d < a.n_out; ++d) {
+          // destinations in an order rotated by the block index: with peers, the CTAs
+          // of a wave then push into every GPU's NVLink ingress at once, not all into one
+          for (int i = 0; i < a.n_out; ++i) {
+            const int d = (i + static_cast<int>(blockIdx.x)) % a.n_out;
             tma_store_3d(&a.tm_out[d], stage, xq, yq, b);
             tma_store_3d(&a.tm_out[d], stage + kQAtom, xq + 64, yq, b);
           }
@@ -638,9 +641,11 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
           // the row goes to every destination: with peer buffers (mapped over
           // NVLink) this epilogue is the all-gather of the head-sharded output
 #pragma unroll 1
-          for (int d = 0; d < a.n_out; ++d)
+          for (int i = 0; i < a.n_out; ++i) {
+            const int d = (i + static_cast<int>(blockIdx.x)) % a.n_out;  // rotated, as the TMA epilogue
 #pragma unroll
             for (int c = 0; c < 4; ++c) st_global_v4(a.out[d] + off + 32 * k + 8 * c, v[c]);
+          }
         }
       }
       }
@@ -913,7 +918,10 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
         const int x = tid / BM;
         const uint32_t stage = sbase + kOffQ + x * kQTile;
         const int xq = (a.out_head0 + h) * D, yq = q0 + x * BM;
-        for (int d = 0; d < a.n_out; ++d) {
+        // destinations in an order rotated by the block index: with peers, the CTAs
+        // of a wave then push into every GPU's NVLink ingress at once, not all into one
+        for (int i = 0; i < a.n_out; ++i) {
+          const int d = (i + static_cast<int>(blockIdx.x)) % a.n_out;
           tma_store_3d(&a.tm_out[d], stage, xq, yq, b);
           tma_store_3d(&a.tm_out[d], stage + kQAtom, xq + 64, yq, b);
         }
