@@ -160,7 +160,10 @@ KVQ_API int kvq_attention_workspace_bytes(int batch, int64_t n_q, int n_heads, i
  * through its own pool and gives a plugin no way to ask for more. No counterpart
  * in the reference (its attention is a library call with no workspace).
  * The workspace is KVQ_NOALLOC_SCRATCH_BYTES of device memory inside the library,
- * one instance per device; no call allocates. The first call on a device looks
+ * one instance per device, held by every GPU that loads the library's device code
+ * until the process exits; no call allocates. It keeps the last call's contents:
+ * each launch first clears the part counters that must start at zero (the partial
+ * results are always written before they are read). The first call on a device looks
  * the scratch up (and loads the library's device code if that has not happened
  * yet): make it before any stream capture. A shape whose workspace would be
  * larger (kvq_attention_workspace_bytes) is rejected with KVQ_ERR_UNSUPPORTED.
