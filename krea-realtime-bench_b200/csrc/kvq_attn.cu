@@ -872,7 +872,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
         // float4s from one part's slot to the next
         const int64_t pstride = (unit < a.split_full ? 2 : 1) * static_cast<int64_t>(33) * BM;
         float wp[kMaxParts];
-        float mx = -INFINITY, L = 0.0f;
+        float mx = -INFINITY, lsum = 0.0f;
 #pragma unroll
         for (int p = 0; p < kMaxParts; ++p)
           if (p < parts) mx = fmaxf(mx, __ldcg(src + p * pstride + 32 * BM).x);
@@ -882,10 +882,10 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
           if (p < parts) {
             const float4 ml = __ldcg(src + p * pstride + 32 * BM);
             wp[p] = ex2(ml.x - mx);
-            L = fmaf(ml.y, wp[p], L);
+            lsum = fmaf(ml.y, wp[p], lsum);
           }
         }
-        const float inv = 1.0f / L;
+        const float inv = 1.0f / lsum;
         const uint32_t stage = sbase + kOffQ + x * kQTile;
 #pragma unroll 1
         for (int ch = 0; ch < 16; ++ch) {  // 8 output channels per 16-byte chunk

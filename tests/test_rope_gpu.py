@@ -81,3 +81,61 @@ def test_rope_quantize_special_values():
     assert np.array_equal(c.packed.cpu().numpy(), codes)
     assert np.array_equal(_u16(c.scales), scales)
     assert np.array_equal(_u16(c.sink), xr[:200])
+
+
+def _near_decision_keys(S, H, t0, tries, seed):
+    """bf16 keys [S, H, 128] whose rotated pairs lie close to a point where
+    bf16(fp32(t)) changes: for each (token, head, pair) the best of `tries` random
+    N(0,1) x log-normal candidates by the distance (in fp32 ulps) of the fp64
+    rotation's real or imaginary part from that point."""
+    from kvq import rope
+    rng = np.random.default_rng(seed)
+    fr = rope.freqs(1024).numpy()
+    pos = rope.grid_positions(t0, S).numpy()
+    axis = np.repeat(np.arange(3), ko.ROPE_SPLIT)
+    cs = fr[np.clip(pos, 0, 1023)[:, axis], np.arange(64)[None, :]]
+    scale = np.exp(rng.standard_normal((H, 64, 1)))
+
+    def dist(t):
+        r = t.astype(np.float32)
+        m = ((r.view(np.uint32) & np.uint32(0xFFFF0000)) | np.uint32(0x8000)).view(np.float32)
+        u = np.spacing(np.abs(m)).astype(np.float64)
+        m = m.astype(np.float64)
+        return np.minimum(np.abs(t - (m - u / 2)), np.abs(t - (m + u / 2))) / u
+
+    out = np.empty((S, H, 128), np.uint16)
+    best = np.empty((S, H, 64))
+    for t in range(S):
+        c, s = cs[t, :, 0][None, :, None], cs[t, :, 1][None, :, None]
+        b0 = ko.f32_to_bf16((rng.standard_normal((H, 64, tries)) * scale).astype(np.float32))
+        b1 = ko.f32_to_bf16((rng.standard_normal((H, 64, tries)) * scale).astype(np.float32))
+        x0, x1 = ko.bf16_to_f32(b0).astype(np.float64), ko.bf16_to_f32(b1).astype(np.float64)
+        d = np.minimum(dist(x0 * c - x1 * s), dist(x0 * s + x1 * c))
+        k = d.argmin(-1)[..., None]
+        best[t] = np.take_along_axis(d, k, -1)[..., 0]
+        out[t, :, 0::2] = np.take_along_axis(b0, k, -1)[..., 0]
+        out[t, :, 1::2] = np.take_along_axis(b1, k, -1)[..., 0]
+    return out, best
+
+
+def test_rope_near_rounding_decision_points():
+    """Keys whose fp64 rotation lands within a few fp32 ulps of a point where
+    bf16(fp32(t)) changes, so that the double rounding (fp64 -> fp32 -> bf16,
+    ties to even on the fp32 value) decides the result: every rotated row, all
+    of them kept in the sink, and the codes and scales stay bit-identical to the
+    oracle."""
+    import quant_kv
+    from kvq import rope
+    S, H, t0 = 32, 4, 4717
+    xb, best = _near_decision_keys(S, H, t0, 1024, seed=11)
+    assert np.mean(best < 8) > 0.25           # the search found hard pairs
+    x = torch.from_numpy(xb.view(np.int16)).view(torch.bfloat16)
+    c = quant_kv.QuantKVTensor([1, S, H, 128], "cuda", torch.bfloat16, 4, "bands4", S)
+    fr = rope.freqs(1024)
+    pos = rope.grid_positions(t0, S)
+    c.write_rope_(0, S, x.unsqueeze(0).cuda(), fr.cuda(), pos.cuda())
+    xr = ko.rope_f64(xb, fr.numpy(), pos.numpy())
+    assert np.array_equal(_u16(c.sink), xr)
+    codes, scales = c_oracle.quantize(xr, ko.band_edges(128, "bands4"))
+    assert np.array_equal(c.packed.cpu().numpy(), codes)
+    assert np.array_equal(_u16(c.scales), scales)
